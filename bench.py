@@ -1,0 +1,432 @@
+"""Benchmark of the KernelSwift-B200 operators (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dsa_e2e|c1|c2|c3|c4]
+                    [--impl ours|reference]
+
+Default workload ``dsa_e2e`` is BASELINE.json's end-to-end DSA configuration (C5):
+the indexer (B=2, S=T=32768, 64 heads x 128, RoPE 64, top-2048, causal) feeding
+sparse attention (128 heads, D=576, dv=512, its int32 indices), plus Sinkhorn on
+(2, 32768, 8, 8) fp32 with 20 iterations.  A step is one pass of the three ops
+over this rank's query rows; rows are sharded over ranks (zigzag for the causal
+indexer, contiguous for the rest) with no collective on the data path, so the
+total work is fixed as N grows (strong scaling).  ``value`` is query tokens per
+second for the whole job (device-resident inputs, CUDA events, max over ranks);
+``e2e`` adds the per-step host<->device copies of the activations (pinned
+memory) through the public ops.  Inputs are seeded synthetic tensors of the
+configuration's shapes and distributions (no dataset is involved).
+
+``--impl reference`` times the reference algorithm on the host cores instead
+(the CPU restatement in oracle/, all threads), on bounded row samples of the
+same workload, extrapolated to the full step; under torchrun only rank 0 runs.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ---------------------------------------------------------------- workloads
+class Workload:
+    name = ""
+    metric = "tokens/s"
+    dtype = "bf16"
+
+    def __init__(self, rank, world, device):
+        self.rank, self.world, self.device = rank, world, device
+
+
+def _freqs(S, rd, pos0=0):
+    import torch
+
+    inv = 1.0 / (10000.0 ** (torch.arange(0, rd, 2, dtype=torch.float32) / rd))
+    ang = torch.outer(torch.arange(pos0, pos0 + S, dtype=torch.float32), inv)
+    return torch.stack([ang.cos(), ang.sin()], -1).contiguous()
+
+
+class DsaE2E(Workload):
+    """C5: indexer -> sparse attention, plus Sinkhorn."""
+    name = "dsa_e2e"
+
+    def __init__(self, rank, world, device, B=2, S=32768, H_ix=64, D_ix=128, rd=64, k=2048,
+                 H_sa=128, D_sa=576, dv=512, sk_shape=(2, 32768, 8, 8), sk_repeat=20):
+        super().__init__(rank, world, device)
+        self.B, self.S, self.H_ix, self.D_ix, self.rd, self.k = B, S, H_ix, D_ix, rd, k
+        self.H_sa, self.D_sa, self.dv = H_sa, D_sa, dv
+        self.sk_shape, self.sk_repeat = sk_shape, sk_repeat
+        self.units = B * S  # query tokens per step, whole job
+        self._host = None
+        if device is None:  # host-only instance (reference arm)
+            return
+        import torch
+        from kernelswift_b200 import ops, shard
+
+        self.ranges = shard.zigzag(S, world, rank)
+        g = torch.Generator(device=device).manual_seed(1234 + rank)
+        dev = device
+        # resident model state (copied once): keys, latent kv, sinks, rope tables
+        self.k_ix = torch.randn(B, S, D_ix, device=dev, generator=g).bfloat16()
+        self.kv = torch.randn(B, S, D_sa, device=dev, generator=g).bfloat16()
+        self.sink = torch.zeros(H_sa, device=dev)
+        self.freqs = [_freqs(b - a, rd, a).to(dev) for a, b in self.ranges]
+        # per-step activations and outputs, one set per row range of this rank
+        self.q_ix, self.w, self.q_sa, self.idx, self.out = [], [], [], [], []
+        for a, b in self.ranges:
+            n = b - a
+            self.q_ix.append(torch.randn(B, n, H_ix, D_ix, device=dev, generator=g).bfloat16())
+            self.w.append((torch.rand(B, n, H_ix, device=dev, generator=g) *
+                           (D_ix ** -0.5 * H_ix ** -0.5)).bfloat16())
+            self.q_sa.append(torch.randn(B, n, H_sa, D_sa, device=dev, generator=g).bfloat16())
+            self.idx.append(torch.empty(B, n, k, dtype=torch.int32, device=dev))
+            self.out.append(torch.empty(B, n, H_sa, dv, dtype=torch.bfloat16, device=dev))
+        n_mats = sk_shape[0] * sk_shape[1]
+        m0, m1 = (shard.contiguous(n_mats, world, rank) or [(0, 0)])[0]
+        self.sk_x = torch.randn(m1 - m0, sk_shape[2], sk_shape[3], device=dev, generator=g)
+        self.sk_out = torch.empty_like(self.sk_x)
+        self.ws = torch.empty(max(ops.indexer_workspace_size(B, b - a, S) for a, b in self.ranges),
+                              dtype=torch.uint8, device=dev)
+
+    def flops(self):
+        """Algorithmic FLOPs per step on this rank (causal-valid pairs for the indexer)."""
+        ix = sum(2 * self.H_ix * self.D_ix * self.B * ((a + 1 + b) * (b - a) // 2)
+                 for a, b in self.ranges)
+        rows = sum(b - a for a, b in self.ranges)
+        sa = 2 * self.B * rows * self.H_sa * self.k * (self.D_sa + self.dv)
+        return {"indexer": ix, "sparse_attn": sa}
+
+    def run(self, timers=None):
+        from kernelswift_b200 import ops
+
+        for i, (a, b) in enumerate(self.ranges):
+            with _span(timers, "indexer"):
+                # rows a..b-1 of a causal prefill over all S keys (row s reads keys t <= s)
+                ops.indexer_topk(self.q_ix[i], self.k_ix, self.w[i], self.freqs[i], self.rd,
+                                 self.S, self.k, 1, True, 0, pos0=a, out=self.idx[i],
+                                 workspace=self.ws)
+            with _span(timers, "sparse_attn"):
+                ops.sparse_attn(self.q_sa[i], self.kv, self.sink, self.idx[i], self.D_sa ** -0.5,
+                                self.dv, out=self.out[i])
+        with _span(timers, "sinkhorn"):
+            ops.sinkhorn(self.sk_x, self.sk_repeat, 1e-6, out=self.sk_out)
+
+    def launches_per_step(self):
+        return 3 * len(self.ranges) + 1  # (score + top-k + attention) per range, Sinkhorn
+
+    def host_buffers(self):
+        import torch
+
+        def pin(t):
+            return torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t)
+
+        if self._host is None:
+            self._host = {"q_ix": [pin(t) for t in self.q_ix], "w": [pin(t) for t in self.w],
+                          "q_sa": [pin(t) for t in self.q_sa], "sk_x": pin(self.sk_x),
+                          "out": [pin(t) for t in self.out], "idx": [pin(t) for t in self.idx],
+                          "sk_out": pin(self.sk_out)}
+        return self._host
+
+    def run_e2e(self):
+        h = self.host_buffers()
+        for name in ("q_ix", "w", "q_sa"):
+            for d, s in zip(getattr(self, name), h[name]):
+                d.copy_(s, non_blocking=True)
+        self.sk_x.copy_(h["sk_x"], non_blocking=True)
+        self.run()
+        for name in ("out", "idx"):
+            for d, s in zip(h[name], getattr(self, name)):
+                d.copy_(s, non_blocking=True)
+        h["sk_out"].copy_(self.sk_out, non_blocking=True)
+
+    def e2e_bytes(self):
+        nb = lambda ts: sum(t.numel() * t.element_size() for t in ts)
+        h2d = nb(self.q_ix) + nb(self.w) + nb(self.q_sa) + nb([self.sk_x])
+        d2h = nb(self.out) + nb(self.idx) + nb([self.sk_out])
+        return h2d, d2h
+
+    def config(self):
+        return {"workload": "C5 end-to-end DSA: indexer(B=2,S=T=32768,H=64,D=128,rope=64,top-2048,"
+                            "causal) -> sparse_attn(H=128,D=576,dv=512) + sinkhorn(2,32768,8,8)x20",
+                "global_batch": self.B, "seq_len": self.S, "parallelism": f"rows{self.world}",
+                "sharding": "zigzag causal row ranges (indexer and attention), contiguous matrices "
+                            "(sinkhorn)",
+                "l2": "inputs larger than L2 (126 MB) every step"}
+
+    # ---- CPU sample of the same workload (oracle restatement)
+    def cpu_sample(self, budget_rows=(8, 8, 8192)):
+        from oracle import ks_oracle as O
+
+        rng = np.random.default_rng(0)
+        n_ix, n_sa, n_sk = budget_rows
+        S = self.S
+        kx = O.f32_to_bf16(rng.standard_normal((1, S, self.D_ix)).astype(np.float32))
+        t_ix = 0.0
+        # rows spread evenly over positions: mean causal cost of the sample ~ of the sequence
+        for s in np.linspace(0, S - 1, n_ix).astype(int):
+            q = O.f32_to_bf16(rng.standard_normal((1, 1, self.H_ix, self.D_ix)).astype(np.float32))
+            w = O.f32_to_bf16(rng.uniform(0, 0.01, (1, 1, self.H_ix)).astype(np.float32))
+            f = _freqs(1, self.rd, int(s)).numpy()
+            t0 = time.perf_counter()
+            O.indexer_forward(q, kx[:, : s + 1], w, f, self.rd, self.k, 1, 0, 0, s0=int(s))
+            t_ix += time.perf_counter() - t0
+        kv = O.f32_to_bf16(rng.standard_normal((1, S, self.D_sa)).astype(np.float32))
+        q = O.f32_to_bf16(rng.standard_normal((1, n_sa, self.H_sa, self.D_sa)).astype(np.float32))
+        idx = np.stack([rng.permutation(S)[: self.k] for _ in range(n_sa)])[None].astype(np.int32)
+        t0 = time.perf_counter()
+        O.sparse_attn(q, kv, np.zeros(self.H_sa, np.float32), idx, self.D_sa ** -0.5, self.dv)
+        t_sa = time.perf_counter() - t0
+        x = rng.standard_normal((n_sk, 8, 8)).astype(np.float32)
+        t0 = time.perf_counter()
+        O.sinkhorn(x, self.sk_repeat, 1e-6)
+        t_sk = time.perf_counter() - t0
+        rows = self.B * S
+        n_mats = self.sk_shape[0] * self.sk_shape[1]
+        t_step = t_ix / n_ix * rows + t_sa / n_sa * rows + t_sk / n_sk * n_mats
+        return rows / t_step, (f"{n_ix} indexer rows spread over positions 0..{S-1}, {n_sa} "
+                               f"sparse-attention rows, {n_sk} Sinkhorn matrices; time per row "
+                               f"extrapolated to the full step")
+
+
+def _span(timers, name):
+    return timers.span(name) if timers is not None else _null()
+
+
+class _null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+class Timers:
+    """CUDA-event spans per kernel family on the current stream."""
+
+    def __init__(self):
+        self.spans = {}
+
+    def span(self, name):
+        import torch
+
+        t = self
+
+        class _S:
+            def __enter__(s):
+                s.a = torch.cuda.Event(enable_timing=True)
+                s.b = torch.cuda.Event(enable_timing=True)
+                s.a.record()
+                return s
+
+            def __exit__(s, *exc):
+                s.b.record()
+                t.spans.setdefault(name, []).append((s.a, s.b))
+                return False
+
+        return _S()
+
+    def per_step_ms(self, steps):
+        """Total device time of each kernel family per step."""
+        return {k: sum(a.elapsed_time(b) for a, b in v) / steps for k, v in self.spans.items()}
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+WORKLOADS = {"dsa_e2e": DsaE2E}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="dsa_e2e", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if a.impl == "reference":
+        return reference_arm(a, rank, world)
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+    wl = WORKLOADS[a.workload](rank, world, device)
+    from kernelswift_b200 import ops
+
+    for _ in range(a.warmup):
+        wl.run()
+    torch.cuda.synchronize()
+    ops.device_status()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-resident timed region
+    clocks = ClockSampler(local)
+    clocks.start()
+    timers = Timers()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        wl.run(timers)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / a.steps
+    clk = clocks.stop()
+    ops.device_status()
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    spans = timers.per_step_ms(a.steps)
+
+    # ---- end to end through the public ops, host buffers
+    e2e = None
+    if not a.no_e2e:
+        wl.host_buffers()
+        wl.run_e2e()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(a.steps):
+            wl.run_e2e()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        t = torch.tensor([e0.elapsed_time(e1) / a.steps], device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        h2d, d2h = wl.e2e_bytes()
+        e2e = {"value": wl.units / (float(t.item()) / 1e3), "unit": wl.metric,
+               "ms_per_step": float(t.item()), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+    peaks = measured_peaks()
+    fl = wl.flops()
+    dom = max(fl, key=fl.get)
+    ach = fl[dom] / (spans[dom] / 1e3) / 1e12
+    peak = peaks["bf16_tflops_sustained"]
+    roofline = {"bound": "tensor", "kernel": dom, "achieved": round(ach, 1), "peak": peak,
+                "unit": "TFLOP/s", "frac": round(ach / peak, 4), "traffic": None,
+                "peak_source": f"{peaks['source']} (sustained bf16)",
+                "per_kernel_ms": {k: round(v, 4) for k, v in spans.items()}}
+    line = {"metric": wl.metric, "value": wl.units / (ms / 1e3), "unit": wl.metric, "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype,
+            "data": "synthetic (seeded, shapes and distributions of the configuration)",
+            "config": wl.config(), "roofline": roofline, "e2e": e2e,
+            "gpu_launches": wl.launches_per_step() * a.steps, "clocks": clk}
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        v, sample = wl.cpu_sample()
+        line["cpu_baseline"] = {"value": v, "unit": wl.metric, "cores": os.cpu_count(),
+                                "kind": "port", "sample": sample}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def reference_arm(a, rank, world):
+    if rank != 0:
+        return
+    wl_cls = WORKLOADS[a.workload]
+    wl = wl_cls(0, world, None)
+    vals = []
+    sample = ""
+    for i in range(a.warmup + a.steps):
+        v, sample = wl.cpu_sample(budget_rows=(4, 4, 4096))
+        if i >= a.warmup:
+            vals.append(v)
+    v = statistics.median(vals)
+    cfg = wl.config()
+    cfg["parallelism"] = "host cores"
+    line = {"impl": "reference", "metric": "tokens/s", "value": v, "unit": "tokens/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": wl.B * wl.S / v * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded)", "config": cfg,
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,139 @@
+/*
+ * KernelSwift-B200: C ABI of the sm_100a operator library (libks_b200.so).
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*, NULL = legacy default stream), launches
+ * asynchronously on that stream and returns KS_OK or an error code; the message
+ * of the last error on the calling thread is available from ks_last_error().
+ * The caller owns all input, output and workspace memory.  Tensors are
+ * row-major and contiguous unless a stride argument says otherwise.  bf16
+ * tensors are passed as raw 16-bit storage.
+ *
+ * Kernels never spin without bound: a wait that runs out of its time budget
+ * (KS_WAIT_BUDGET_MS in the environment, default 2000 ms) records an error in a
+ * per-device status word and the kernel returns.  ks_device_status() reads and
+ * clears that word.
+ */
+#ifndef KS_B200_H
+#define KS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KS_OK 0
+#define KS_ERR_INVALID 1     /* bad pointer, shape or argument */
+#define KS_ERR_UNSUPPORTED 2 /* valid call outside what the kernels implement */
+#define KS_ERR_ALIGNMENT 3   /* pointer or stride not aligned as required */
+#define KS_ERR_CUDA 4        /* a CUDA runtime call failed */
+#define KS_ERR_WORKSPACE 5   /* workspace missing or too small */
+#define KS_ERR_DEVICE 6      /* a kernel reported a timed-out wait or a bounds error */
+
+#define KS_INT32 0
+#define KS_INT64 1
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* ks_last_error(void);
+
+/* Library ABI version (major * 100 + minor). */
+int ks_version(void);
+
+/*
+ * Sinkhorn normalisation of n_mats independent n x n fp32 matrices (x and out
+ * are [n_mats, n, n], 16-byte aligned; x == out is allowed).
+ * Semantics of baseline/sinkhorn.py:13-19: softmax over the last dim plus eps,
+ * one column normalisation, then repeat-1 (row, column) normalisations, each
+ * dividing by (sum + eps).  1 <= n <= 64.
+ * Replaces sinkhorn_torch, optimized/sinkhorn_project/op_extension/sinkhorn_torch.cpp:18-56
+ * (which accepted 4x4 only).
+ */
+int ks_sinkhorn(const float* x, float* out, int64_t n_mats, int32_t n, int32_t repeat, float eps,
+                void* stream);
+
+/*
+ * Top-k sparse attention with a per-head sink logit, baseline/sparse_attention.py:5-42.
+ *   q    bf16 [B, M, H, D]     kv bf16 [B, N, D] (shared by all heads: MQA / MLA latent)
+ *   sink fp32 [H]              topk_idxs int32 [B, M, K]; entries < 0 are ignored,
+ *                              repeated entries count once per occurrence
+ *   out  bf16 [B, M, H, dv]  = output columns [dv_begin, dv_begin + dv) of the
+ *                              reference (V is kv[..., dv_begin : dv_begin + dv]).
+ * Requirements: H <= 128, D % 64 == 0, D <= 576, dv % 64 == 0 (dv may be any
+ * multiple of 64 up to 512), dv_begin % 64 == 0, dv_begin + dv <= D, idx < N.
+ * Replaces sparse_attn_megakernel_basic_torch,
+ * optimized/sparse_attention/op_extension/sparse_attn_torch.cpp:96-160.
+ */
+int ks_sparse_attn(const void* q, const void* kv, const float* attn_sink,
+                   const int32_t* topk_idxs, void* out, int64_t B, int64_t M, int64_t H,
+                   int64_t D, int64_t N, int64_t K, int64_t dv_begin, int64_t dv,
+                   float softmax_scale, void* stream);
+
+/* Workspace bytes ks_indexer needs for B x S query rows over T keys. */
+size_t ks_indexer_workspace_size(int64_t B, int64_t S, int64_t T);
+
+/*
+ * Lightning-indexer top-k, baseline/indexer.py:170-205 after the two projections:
+ * RoPE on the last rope_dim dims of q, scores
+ *   bf16( sum_h bf16( relu(bf16(q_h . k_t)) * w_h ) ),
+ * causal mask (causal != 0: key t valid iff t < (pos0 + s + 1) / ratio),
+ * top-min(topk, T) indices by value descending, ties by lower index, then
+ * causal: invalid -> -1, else index + offset.
+ *   q     bf16 [B, S, H, D], projected, before RoPE      (H in {16, 32, 64}, D in {64, 128})
+ *   k     bf16 keys; batch b, key t at k + (b * k_batch_rows + t) * D   (t < T <= 65536)
+ *   w     bf16 [B, S, H] head weights (already scaled by D^-0.5 H^-0.5)
+ *   freqs fp32 [S, rope_dim / 2, 2] (cos, sin) at the positions of the S rows
+ *   out   [B, S, min(topk, T)] int32 (out_dtype KS_INT32) or int64 (KS_INT64)
+ *   pos0  sequence position of row s = 0 (0 for a whole prefill call; the
+ *         first row of the shard when the rows are split)
+ * topk <= 4096.  workspace >= ks_indexer_workspace_size(B, S, T), 256-byte aligned.
+ * Replaces indexer_rope_torch, indexer_qk_reduce_torch and indexer_topk_torch,
+ * optimized/indexer_project/op_extension/indexer_torch.cpp:100-268.
+ */
+int ks_indexer(const void* q, const void* k, int64_t k_batch_rows, const void* w,
+               const float* freqs, int64_t B, int64_t S, int64_t H, int64_t D, int64_t T,
+               int32_t rope_dim, int64_t pos0, int32_t causal, int32_t ratio, int32_t topk,
+               int64_t offset, void* out, int32_t out_dtype, void* workspace,
+               size_t workspace_bytes, void* stream);
+
+/*
+ * Score stage of ks_indexer alone: writes bf16 scores [B * S, score_ld] (row
+ * b * S + s; columns >= the row's causal limit inside the last 128-key tile
+ * hold -inf, columns beyond it are not written).  score_ld % 8 == 0, >= T.
+ * Replaces indexer_rope_torch + indexer_qk_reduce_torch,
+ * optimized/indexer_project/op_extension/indexer_torch.cpp:100-198.
+ */
+int ks_indexer_scores(const void* q, const void* k, int64_t k_batch_rows, const void* w,
+                      const float* freqs, int64_t B, int64_t S, int64_t H, int64_t D, int64_t T,
+                      int32_t rope_dim, int64_t pos0, int32_t causal, int32_t ratio,
+                      void* scores, int64_t score_ld, void* stream);
+
+/*
+ * Top-k stage of ks_indexer alone over bf16 score rows [B * S, score_ld]
+ * (only the valid prefix of each row is read).
+ * Replaces indexer_topk_torch, optimized/indexer_project/op_extension/indexer_torch.cpp:232-268.
+ */
+int ks_topk_rows(const void* scores, int64_t score_ld, int64_t B, int64_t S, int64_t T,
+                 int64_t pos0, int32_t causal, int32_t ratio, int32_t topk, int64_t offset,
+                 void* out, int32_t out_dtype, void* stream);
+
+/*
+ * Synchronise `stream`, then read and clear the current device's status word:
+ * KS_OK, or KS_ERR_DEVICE when a kernel reported a timed-out wait or a bounds
+ * error since the last call.  No counterpart in the reference.
+ */
+int ks_device_status(void* stream);
+
+/*
+ * Self-test of the bounded-wait path: launches one CTA that waits on a barrier
+ * nobody completes, with the given budget; the wait gives up, records a
+ * timeout in the status word and the kernel returns.  No counterpart in the
+ * reference.
+ */
+int ks_selftest_wait_timeout(uint64_t budget_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KS_B200_H */

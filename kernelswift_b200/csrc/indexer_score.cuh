@@ -1,0 +1,297 @@
+// Indexer scores on tcgen05: RoPE fused into the query-tile load, the q.k GEMM on
+// the tensor cores with TMEM accumulators, and the bf16-exact epilogue.
+//
+// Semantics follow baseline/indexer.py:170-193 of KernelSwift (the NPU version is
+// optimized/indexer_project/op_kernel/fused_indexer_qk_reduce.asc:368-428):
+//   score[b,s,t] = bf16( sum_h bf16( relu(bf16(q[b,s,h,:] . k[b,t,:])) * w[b,s,h] ) )
+// with the head sum in fp32 in head order, and t >= (s+1)//ratio masked to -inf
+// for causal prefill rows.  RoPE rotates the last `rd` dims of q (interleaved
+// pairs, fp32 products and sums rounded separately, result rounded to bf16),
+// baseline/indexer.py:114-129,172.
+//
+// GEMM orientation: keys are the M dimension (128 per tile) and (token, head) is
+// the N dimension (tok = 256/H tokens x H heads = 256).  The head reduction is
+// therefore along TMEM columns, i.e. inside one thread: TMEM lane = key.
+//
+// Persistent CTAs, one per SM, 12 warps:
+//   warp 0      TMA producer: query tiles (2 buffers) and key tiles (KST stages)
+//   warp 1      TMEM owner and MMA issuer (one elected lane)
+//   warps 2-3   RoPE on the query tile in shared memory (swizzled layout)
+//   warps 4-11  epilogue: TMEM -> registers -> bf16 chain -> global scores
+// Accumulators: 2 x 256 TMEM columns (double buffered), 512 columns in total.
+// Work items (batch, token group) are handed out heaviest-first (causal cost
+// grows with the position), strided over CTAs.
+#pragma once
+#include "ks_device.cuh"
+
+namespace ks {
+
+constexpr int IX_THREADS = 384;
+constexpr int IX_EPI_WARP0 = 4;
+constexpr int IX_EPI_THREADS = 256;
+constexpr int IX_ROPE_THREADS = 64;
+constexpr int IX_TILE_KEYS = 128;
+constexpr int IX_N = 256;
+constexpr int IX_MAX_KST = 8;
+
+struct IndexerScoreParams {
+  const float* freqs;  // [S, rd/2, 2] (cos, sin) for the rows' positions
+  const uint16_t* w;   // bf16 [B, S, H] (batch stride w_bs elements)
+  int64_t w_bs;
+  uint16_t* scores;    // bf16 [B*S, score_ld]
+  int64_t score_ld;
+  int32_t B, S, H, D, T, rd;
+  int64_t k_rows_per_batch;  // rows between batches in the key tensor map
+  int64_t pos0;              // sequence position of row s = 0
+  int32_t causal, ratio;
+  int32_t tok, n_groups, n_items, kst;
+  int* status;
+  uint64_t budget_ns;
+};
+
+struct IxShared {
+  uint64_t k_full[IX_MAX_KST], k_empty[IX_MAX_KST];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t q_tma[2], q_full[2], q_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ int ix_item_tiles(const IndexerScoreParams& p, int item, int& b,
+                                             int& g) {
+  g = p.n_groups - 1 - item / p.B;
+  b = item % p.B;
+  int s_last = g * p.tok + p.tok - 1;
+  if (s_last > p.S - 1) s_last = p.S - 1;
+  int64_t kmax = p.T;
+  if (p.causal) {
+    const int64_t lim = (p.pos0 + s_last + 1) / p.ratio;
+    kmax = lim < kmax ? lim : kmax;
+  }
+  if (kmax < 0) kmax = 0;
+  return (int)((kmax + IX_TILE_KEYS - 1) / IX_TILE_KEYS);
+}
+
+template <int H>
+__global__ void __launch_bounds__(IX_THREADS, 1)
+    indexer_score_kernel(const __grid_constant__ CUtensorMap qmap,
+                         const __grid_constant__ CUtensorMap kmap, IndexerScoreParams p) {
+  extern __shared__ uint8_t ix_raw[];
+  const uint32_t raw_addr = smem_u32(ix_raw);
+  uint8_t* smem = ix_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  // layout: [IxShared, padded to 1 KB][2 query tiles][kst key stages], 1 KB aligned
+  const int D = p.D;
+  const uint32_t q_bytes = (uint32_t)IX_N * D * 2;         // one query tile
+  const uint32_t k_bytes = (uint32_t)IX_TILE_KEYS * D * 2;  // one key stage
+  IxShared* sh = reinterpret_cast<IxShared*>(smem);
+  uint8_t* qbuf = smem + 1024;
+  uint8_t* kbuf = qbuf + 2 * q_bytes;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  WaitCtx wc{&sh->abort, p.status, p.budget_ns};
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.kst; ++i) {
+      mbar_init(&sh->k_full[i], 1);
+      mbar_init(&sh->k_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh->acc_full[i], 1);
+      mbar_init(&sh->acc_empty[i], IX_EPI_THREADS / 32);
+      mbar_init(&sh->q_tma[i], 1);
+      mbar_init(&sh->q_full[i], IX_ROPE_THREADS);
+      mbar_init(&sh->q_empty[i], 1);
+    }
+    mbar_init(&sh->drain, 1);
+    sh->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<1>(&sh->tmem_base, 512);
+    tmem_relinquish<1>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&qmap);
+      tma_prefetch_desc(&kmap);
+      uint32_t kc = 0, qc = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+        int b, g;
+        const int nt = ix_item_tiles(p, item, b, g);
+        if (nt == 0) continue;
+        const int qs = qc & 1;
+        if (!(ok = mbar_wait(&sh->q_empty[qs], ((qc >> 1) & 1) ^ 1, wc))) break;
+        mbar_expect_tx(&sh->q_tma[qs], q_bytes);
+        const int32_t qrow = (int32_t)(((int64_t)b * p.S + (int64_t)g * p.tok) * p.H);
+        for (int kb = 0; kb < D / 64; ++kb)
+          tma_load_2d(&qmap, &sh->q_tma[qs], qbuf + qs * q_bytes + kb * (IX_N * 128), kb * 64,
+                      qrow);
+        ++qc;
+        for (int t = 0; t < nt; ++t) {
+          const int st = kc % p.kst;
+          if (!(ok = mbar_wait(&sh->k_empty[st], ((kc / p.kst) & 1) ^ 1, wc))) break;
+          mbar_expect_tx(&sh->k_full[st], k_bytes);
+          const int32_t krow = (int32_t)(b * p.k_rows_per_batch + t * IX_TILE_KEYS);
+          for (int kb = 0; kb < D / 64; ++kb)
+            tma_load_2d(&kmap, &sh->k_full[st], kbuf + st * k_bytes + kb * (IX_TILE_KEYS * 128),
+                        kb * 64, krow);
+          ++kc;
+        }
+      }
+      // drain: wait for every load this thread issued (bounded)
+      for (uint32_t i = (kc > (uint32_t)p.kst ? kc - p.kst : 0); i < kc; ++i)
+        mbar_wait(&sh->k_full[i % p.kst], (i / p.kst) & 1, wc, false, true);
+      for (uint32_t i = (qc > 2 ? qc - 2 : 0); i < qc; ++i)
+        mbar_wait(&sh->q_tma[i & 1], (i >> 1) & 1, wc, false, true);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(IX_TILE_KEYS, IX_N, false, false);
+      uint32_t kc = 0, qc = 0, ac = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+        int b, g;
+        const int nt = ix_item_tiles(p, item, b, g);
+        if (nt == 0) continue;
+        const int qs = qc & 1;
+        if (!(ok = mbar_wait(&sh->q_full[qs], (qc >> 1) & 1, wc))) break;
+        const uint32_t qaddr = smem_u32(qbuf + qs * q_bytes);
+        for (int t = 0; t < nt; ++t) {
+          const int st = kc % p.kst, as = ac & 1;
+          if (!(ok = mbar_wait(&sh->acc_empty[as], ((ac >> 1) & 1) ^ 1, wc))) break;
+          if (!(ok = mbar_wait(&sh->k_full[st], (kc / p.kst) & 1, wc))) break;
+          tc_fence_after();
+          const uint32_t kaddr = smem_u32(kbuf + st * k_bytes);
+          const uint32_t d_tmem = tmem + as * IX_N;
+          for (int kb = 0; kb < D / 64; ++kb) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = sdesc_sw128(kaddr + kb * (IX_TILE_KEYS * 128) + kk * 32, 16, 1024);
+              const uint64_t bd = sdesc_sw128(qaddr + kb * (IX_N * 128) + kk * 32, 16, 1024);
+              umma_bf16_ss(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+            }
+          }
+          umma_commit(&sh->k_empty[st]);
+          umma_commit(&sh->acc_full[as]);
+          ++kc;
+          ++ac;
+        }
+        if (!ok) break;
+        umma_commit(&sh->q_empty[qs]);
+        ++qc;
+      }
+      umma_commit(&sh->drain);
+      mbar_wait(&sh->drain, 0, wc, false, true);
+    }
+  } else if (warp < IX_EPI_WARP0) {
+    // ------------------------------------------------------------ RoPE on the query tile
+    const int t = threadIdx.x - 64;
+    const int rd = p.rd;
+    const int cpr = rd / 8;           // 16-byte chunks per row inside the rope segment
+    const int c0 = (D - rd) / 8;      // first rope chunk of a row
+    uint32_t qc = 0;
+    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+      int b, g;
+      const int nt = ix_item_tiles(p, item, b, g);
+      if (nt == 0) continue;
+      const int qs = qc & 1;
+      if (!mbar_wait(&sh->q_tma[qs], (qc >> 1) & 1, wc)) break;
+      uint8_t* qt = qbuf + qs * q_bytes;
+      for (int id = t; id < IX_N * cpr; id += IX_ROPE_THREADS) {
+        const int n = id / cpr, cc = id % cpr;
+        const int s = g * p.tok + n / p.H;
+        if (s >= p.S) continue;
+        const int cid = c0 + cc;
+        uint8_t* a = qt + (cid >> 3) * (IX_N * 128) + n * 128 + (((cid & 7) ^ (n & 7)) << 4);
+        uint4 v = *reinterpret_cast<uint4*>(a);
+        const float4* f = reinterpret_cast<const float4*>(p.freqs + ((int64_t)s * (rd / 2) + cc * 4) * 2);
+        const float4 f01 = __ldg(f), f23 = __ldg(f + 1);
+        const float cs[4] = {f01.x, f01.z, f23.x, f23.z};
+        const float sn[4] = {f01.y, f01.w, f23.y, f23.w};
+        uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float xr = bf16lo_f32(w4[q]), xi = bf16hi_f32(w4[q]);
+          const float re = __fsub_rn(__fmul_rn(xr, cs[q]), __fmul_rn(xi, sn[q]));
+          const float im = __fadd_rn(__fmul_rn(xr, sn[q]), __fmul_rn(xi, cs[q]));
+          w4[q] = cvt_bf16x2(re, im);
+        }
+        *reinterpret_cast<uint4*>(a) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&sh->q_full[qs]);
+      ++qc;
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int e = warp - IX_EPI_WARP0;  // 0..7
+    const int quarter = warp & 3;       // TMEM lanes [32*quarter, +32) belong to this warp
+    const int half = e >> 2;            // which half of the item's tokens
+    constexpr int TOK = IX_N / H;
+    constexpr int TOK_HALF = TOK / 2;
+    uint32_t ac = 0;
+    for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
+      int b, g;
+      const int nt = ix_item_tiles(p, item, b, g);
+      if (nt == 0) continue;
+      bool ok = true;
+      for (int t = 0; t < nt; ++t) {
+        const int as = ac & 1;
+        if (!(ok = mbar_wait(&sh->acc_full[as], (ac >> 1) & 1, wc))) break;
+        tc_fence_after();
+        const int key = t * IX_TILE_KEYS + quarter * 32 + lane;
+#pragma unroll 1
+        for (int jj = 0; jj < TOK_HALF; ++jj) {
+          const int j = half * TOK_HALF + jj;
+          const int s = g * TOK + j;
+          // head weights of token s as bf16 pairs (warp-uniform loads, L1 resident)
+          const uint32_t* w2 = reinterpret_cast<const uint32_t*>(
+              p.w + (int64_t)b * p.w_bs + (int64_t)(s < p.S ? s : p.S - 1) * H);
+          const uint32_t col = tmem + as * IX_N + j * H + ((uint32_t)(quarter * 32) << 16);
+          uint32_t r[H];
+#pragma unroll
+          for (int c = 0; c < H; c += 16) tmem_ld16(col + c, r + c);
+          tmem_wait_ld();
+          float acc = 0.f;
+#pragma unroll
+          for (int h = 0; h < H; h += 2) {
+            uint32_t pr = cvt_relu_bf16x2(__uint_as_float(r[h]), __uint_as_float(r[h + 1]));
+            pr = mul_bf16x2(pr, __ldg(w2 + (h >> 1)));
+            acc = __fadd_rn(acc, bf16lo_f32(pr));
+            acc = __fadd_rn(acc, bf16hi_f32(pr));
+          }
+          int64_t lim = p.T;
+          if (p.causal) {
+            const int64_t l2 = (p.pos0 + s + 1) / p.ratio;
+            lim = l2 < lim ? l2 : lim;
+          }
+          uint16_t out = __bfloat16_as_ushort(__float2bfloat16_rn(acc));
+          if (key >= lim) out = 0xFF80;  // -inf
+          if (s < p.S && key < p.T)
+            p.scores[((int64_t)b * p.S + s) * p.score_ld + key] = out;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh->acc_empty[as]);
+        ++ac;
+      }
+      if (!ok) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc<1>(tmem, 512);
+}
+
+}  // namespace ks

@@ -1,0 +1,396 @@
+// Host side of libks_b200.so: argument validation, TMA descriptor encoding,
+// launches and the device status word.  The extern "C" functions are declared in
+// include/ks_b200.h.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+#include <string>
+
+#include "ks_b200.h"
+#include "ks_device.cuh"
+#include "indexer_score.cuh"
+#include "sinkhorn.cuh"
+#include "sparse_attn.cuh"
+#include "topk.cuh"
+
+namespace ks {
+
+// Per-device status word written by kernels whose bounded waits ran out.
+__device__ int g_status_word;
+
+namespace {
+
+thread_local std::string t_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(KS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct Device {
+  bool ready = false;
+  int* status = nullptr;  // address of g_status_word on this device
+  int num_sms = 0;
+};
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+Device g_devices[kMaxDevices];
+
+int device(Device** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(KS_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  Device& d = g_devices[dev];
+  if (!d.ready) {
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.status), g_status_word);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    d.ready = true;
+  }
+  *out = &d;
+  return KS_OK;
+}
+
+uint64_t wait_budget_ns() {
+  static uint64_t budget = [] {
+    const char* s = getenv("KS_WAIT_BUDGET_MS");
+    long ms = s ? atol(s) : 2000;
+    if (ms < 1) ms = 1;
+    return (uint64_t)ms * 1000000ull;
+  }();
+  return budget;
+}
+
+int launch_check(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return KS_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// bf16 2D tensor map [rows, inner] with a row stride, 128-byte swizzle, box
+// (box_inner x box_rows).  Rows beyond `rows` read as zero.
+int make_map_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(KS_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return KS_OK;
+}
+
+int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+
+// ------------------------------------------------------------------ indexer helpers
+struct IndexerGeom {
+  int tok, n_groups, n_items, kst;
+  size_t smem;
+};
+
+int indexer_geom(int64_t B, int64_t S, int64_t H, int64_t D, IndexerGeom* g) {
+  g->tok = (int)(IX_N / H);
+  g->n_groups = (int)((S + g->tok - 1) / g->tok);
+  g->n_items = (int)(B * g->n_groups);
+  const size_t q_bytes = (size_t)IX_N * D * 2, k_bytes = (size_t)IX_TILE_KEYS * D * 2;
+  const size_t fixed = 1024 /* alignment slack */ + 2 * q_bytes;
+  const size_t limit = 232448;  // 227 KB opt-in maximum per CTA on sm_100
+  const size_t hdr = 1024;      // IxShared, padded
+  int kst = (int)((limit - fixed - hdr) / k_bytes);
+  if (kst > 4) kst = 4;
+  if (kst < 2) return fail(KS_ERR_UNSUPPORTED, "indexer: D=%lld leaves no room for key stages", (long long)D);
+  g->kst = kst;
+  g->smem = fixed + hdr + (size_t)kst * k_bytes;
+  return KS_OK;
+}
+
+int indexer_check(const void* q, const void* k, const void* w, const float* freqs, int64_t B,
+                  int64_t S, int64_t H, int64_t D, int64_t T, int32_t rope_dim, int32_t ratio,
+                  int64_t k_batch_rows) {
+  if (!q || !k || !w) return fail(KS_ERR_INVALID, "indexer: null input pointer");
+  if (B < 1 || S < 1 || T < 0) return fail(KS_ERR_INVALID, "indexer: bad sizes B=%lld S=%lld T=%lld", (long long)B, (long long)S, (long long)T);
+  if (!(H == 16 || H == 32 || H == 64)) return fail(KS_ERR_UNSUPPORTED, "indexer: H=%lld (supported: 16, 32, 64)", (long long)H);
+  if (!(D == 64 || D == 128)) return fail(KS_ERR_UNSUPPORTED, "indexer: D=%lld (supported: 64, 128)", (long long)D);
+  if (T > 65536) return fail(KS_ERR_UNSUPPORTED, "indexer: T=%lld > 65536", (long long)T);
+  if (rope_dim < 0 || rope_dim > D || rope_dim % 8) return fail(KS_ERR_INVALID, "indexer: rope_dim=%d must be a multiple of 8 in [0, D]", rope_dim);
+  if (rope_dim > 0 && !freqs) return fail(KS_ERR_INVALID, "indexer: freqs is null");
+  if (ratio < 1) return fail(KS_ERR_INVALID, "indexer: ratio=%d", ratio);
+  if (k_batch_rows < T) return fail(KS_ERR_INVALID, "indexer: k_batch_rows < T");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(w, 4) || (freqs && !aligned(freqs, 16)))
+    return fail(KS_ERR_ALIGNMENT, "indexer: q, k, freqs must be 16-byte and w 4-byte aligned");
+  if (B * S * H >= (1ll << 31) || B * k_batch_rows >= (1ll << 31))
+    return fail(KS_ERR_UNSUPPORTED, "indexer: too many rows for 32-bit TMA coordinates");
+  return KS_OK;
+}
+
+template <int H>
+int launch_indexer_scores(const CUtensorMap& qm, const CUtensorMap& km, const IndexerScoreParams& p,
+                          const IndexerGeom& g, int grid, cudaStream_t st) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(indexer_score_kernel<H>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(indexer)");
+  indexer_score_kernel<H><<<grid, IX_THREADS, g.smem, st>>>(qm, km, p);
+  return launch_check("indexer_score_kernel launch");
+}
+
+int indexer_scores_impl(const void* q, const void* k, int64_t k_batch_rows, const void* w,
+                        const float* freqs, int64_t B, int64_t S, int64_t H, int64_t D,
+                        int64_t T, int32_t rope_dim, int64_t pos0, int32_t causal,
+                        int32_t ratio, void* scores, int64_t score_ld, cudaStream_t st) {
+  Device* dev;
+  if (int rc = device(&dev)) return rc;
+  IndexerGeom g;
+  if (int rc = indexer_geom(B, S, H, D, &g)) return rc;
+  if (T == 0) return KS_OK;
+  CUtensorMap qm, km;
+  if (int rc = make_map_bf16(&qm, q, D, (uint64_t)(B * S * H), D * 2, 64, IX_N)) return rc;
+  if (int rc = make_map_bf16(&km, k, D, (uint64_t)(B * k_batch_rows), D * 2, 64, IX_TILE_KEYS)) return rc;
+  IndexerScoreParams p{};
+  p.freqs = freqs;
+  p.w = static_cast<const uint16_t*>(w);
+  p.w_bs = S * H;
+  p.scores = static_cast<uint16_t*>(scores);
+  p.score_ld = score_ld;
+  p.B = (int)B; p.S = (int)S; p.H = (int)H; p.D = (int)D; p.T = (int)T; p.rd = rope_dim;
+  p.k_rows_per_batch = k_batch_rows;
+  p.pos0 = pos0;
+  p.causal = causal ? 1 : 0;
+  p.ratio = ratio;
+  p.tok = g.tok; p.n_groups = g.n_groups; p.n_items = g.n_items; p.kst = g.kst;
+  p.status = dev->status;
+  p.budget_ns = wait_budget_ns();
+  const int grid = g.n_items < dev->num_sms ? g.n_items : dev->num_sms;
+  switch (H) {
+    case 16: return launch_indexer_scores<16>(qm, km, p, g, grid, st);
+    case 32: return launch_indexer_scores<32>(qm, km, p, g, grid, st);
+    default: return launch_indexer_scores<64>(qm, km, p, g, grid, st);
+  }
+}
+
+int topk_impl(const void* scores, int64_t score_ld, int64_t B, int64_t S, int64_t T,
+              int64_t pos0, int32_t causal, int32_t ratio, int32_t topk, int64_t offset,
+              void* out, int32_t out_dtype, cudaStream_t st) {
+  Device* dev;
+  if (int rc = device(&dev)) return rc;
+  if (!scores || !out) return fail(KS_ERR_INVALID, "topk: null pointer");
+  if (B < 1 || S < 1 || T < 0 || topk < 0) return fail(KS_ERR_INVALID, "topk: bad sizes");
+  if (T > 65536) return fail(KS_ERR_UNSUPPORTED, "topk: T=%lld > 65536", (long long)T);
+  if (topk > 4096) return fail(KS_ERR_UNSUPPORTED, "topk: k=%d > 4096", topk);
+  if (score_ld < T || score_ld % 8) return fail(KS_ERR_INVALID, "topk: score_ld must be >= T and a multiple of 8");
+  if (!aligned(scores, 16)) return fail(KS_ERR_ALIGNMENT, "topk: scores must be 16-byte aligned");
+  if (ratio < 1) return fail(KS_ERR_INVALID, "topk: ratio=%d", ratio);
+  if (out_dtype != KS_INT32 && out_dtype != KS_INT64) return fail(KS_ERR_INVALID, "topk: out_dtype");
+  const int K = (int)(topk < T ? topk : T);
+  if (K == 0) return KS_OK;
+  int kpow2 = 1;
+  while (kpow2 < K) kpow2 <<= 1;
+  TopkParams p{};
+  p.scores = static_cast<const uint16_t*>(scores);
+  p.row_stride = score_ld;
+  p.rows = B * S;
+  p.S = S;
+  p.pos0 = pos0;
+  p.causal = causal ? 1 : 0;
+  p.ratio = ratio;
+  p.T = (int)T;
+  p.k = K;
+  p.offset = offset;
+  p.out = out;
+  p.out_i64 = out_dtype == KS_INT64;
+  p.out_row_stride = K;
+  p.kpow2 = kpow2;
+  p.status = dev->status;
+  const size_t smem = (size_t)kpow2 * 4 + (256 + 256 + TK_WARPS + 4 + 8) * 4 + round_up(T, 8) * 2;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(topk)");
+  if (B * S > 0x7FFFFFFFll) return fail(KS_ERR_UNSUPPORTED, "topk: too many rows");
+  topk_rows_kernel<<<(unsigned)(B * S), TK_THREADS, smem, st>>>(p);
+  return launch_check("topk_rows_kernel launch");
+}
+
+__global__ void selftest_wait_kernel(int* status, uint64_t budget_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    WaitCtx w{&abort_flag, status, budget_ns};
+    mbar_wait(&bar, 0, w);  // nobody arrives: gives up after budget_ns
+    mbar_arrive(&bar);      // complete the phase so the barrier is left consistent
+  }
+}
+
+}  // namespace
+}  // namespace ks
+
+using namespace ks;
+
+extern "C" {
+
+const char* ks_last_error(void) { return t_err.c_str(); }
+
+int ks_version(void) { return 100; }
+
+int ks_sinkhorn(const float* x, float* out, int64_t n_mats, int32_t n, int32_t repeat, float eps,
+                void* stream) {
+  Device* dev;
+  if (int rc = device(&dev)) return rc;
+  if (!x || !out) return fail(KS_ERR_INVALID, "sinkhorn: null pointer");
+  if (n_mats < 0 || n < 1) return fail(KS_ERR_INVALID, "sinkhorn: bad sizes");
+  if (n > 64) return fail(KS_ERR_UNSUPPORTED, "sinkhorn: n=%d > 64", n);
+  if (!aligned(x, 16) || !aligned(out, 16)) return fail(KS_ERR_ALIGNMENT, "sinkhorn: pointers must be 16-byte aligned");
+  if (n_mats == 0) return KS_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t blocks_reg = (n_mats + SK_THREADS - 1) / SK_THREADS;
+  auto launch_reg = [&](auto kern, int N) {
+    const size_t smem = (size_t)SK_THREADS * (N * N + 1) * 4;
+    kern<<<(unsigned)blocks_reg, SK_THREADS, smem, st>>>(x, out, n_mats, repeat, eps);
+  };
+  if (blocks_reg > 0x7FFFFFFFll) return fail(KS_ERR_UNSUPPORTED, "sinkhorn: too many matrices");
+  switch (n) {
+    case 1: launch_reg(sinkhorn_reg_kernel<1>, 1); break;
+    case 2: launch_reg(sinkhorn_reg_kernel<2>, 2); break;
+    case 3: launch_reg(sinkhorn_reg_kernel<3>, 3); break;
+    case 4: launch_reg(sinkhorn_reg_kernel<4>, 4); break;
+    case 5: launch_reg(sinkhorn_reg_kernel<5>, 5); break;
+    case 6: launch_reg(sinkhorn_reg_kernel<6>, 6); break;
+    case 7: launch_reg(sinkhorn_reg_kernel<7>, 7); break;
+    case 8: launch_reg(sinkhorn_reg_kernel<8>, 8); break;
+    default: {
+      static std::once_flag once;
+      std::call_once(once, [] {
+        cudaFuncSetAttribute(sinkhorn_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+      });
+      const size_t smem = (size_t)SKW_WARPS * n * (n + 1) * 4;
+      const int64_t blocks = (n_mats + SKW_WARPS - 1) / SKW_WARPS;
+      sinkhorn_warp_kernel<<<(unsigned)blocks, SKW_WARPS * 32, smem, st>>>(x, out, n_mats, n, repeat, eps);
+    }
+  }
+  return launch_check("sinkhorn kernel launch");
+}
+
+size_t ks_indexer_workspace_size(int64_t B, int64_t S, int64_t T) {
+  if (B < 1 || S < 1 || T < 1) return 256;
+  return (size_t)round_up(B * S * round_up(T, 8) * 2, 256);
+}
+
+int ks_indexer_scores(const void* q, const void* k, int64_t k_batch_rows, const void* w,
+                      const float* freqs, int64_t B, int64_t S, int64_t H, int64_t D, int64_t T,
+                      int32_t rope_dim, int64_t pos0, int32_t causal, int32_t ratio,
+                      void* scores, int64_t score_ld, void* stream) {
+  if (int rc = indexer_check(q, k, w, freqs, B, S, H, D, T, rope_dim, ratio, k_batch_rows)) return rc;
+  if (!scores || score_ld < T || score_ld % 8 || !aligned(scores, 16))
+    return fail(KS_ERR_INVALID, "indexer_scores: scores must be 16-byte aligned with score_ld >= T, multiple of 8");
+  return indexer_scores_impl(q, k, k_batch_rows, w, freqs, B, S, H, D, T, rope_dim, pos0, causal,
+                             ratio, scores, score_ld, static_cast<cudaStream_t>(stream));
+}
+
+int ks_topk_rows(const void* scores, int64_t score_ld, int64_t B, int64_t S, int64_t T,
+                 int64_t pos0, int32_t causal, int32_t ratio, int32_t topk, int64_t offset,
+                 void* out, int32_t out_dtype, void* stream) {
+  return topk_impl(scores, score_ld, B, S, T, pos0, causal, ratio, topk, offset, out, out_dtype,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int ks_indexer(const void* q, const void* k, int64_t k_batch_rows, const void* w,
+               const float* freqs, int64_t B, int64_t S, int64_t H, int64_t D, int64_t T,
+               int32_t rope_dim, int64_t pos0, int32_t causal, int32_t ratio, int32_t topk,
+               int64_t offset, void* out, int32_t out_dtype, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  if (int rc = indexer_check(q, k, w, freqs, B, S, H, D, T, rope_dim, ratio, k_batch_rows)) return rc;
+  if (topk < 1 || topk > 4096) return fail(KS_ERR_UNSUPPORTED, "indexer: topk=%d (1..4096)", topk);
+  if (!out) return fail(KS_ERR_INVALID, "indexer: out is null");
+  if (T == 0) return KS_OK;
+  const size_t need = ks_indexer_workspace_size(B, S, T);
+  if (!workspace || workspace_bytes < need)
+    return fail(KS_ERR_WORKSPACE, "indexer: workspace of %zu bytes needed", need);
+  if (!aligned(workspace, 256)) return fail(KS_ERR_ALIGNMENT, "indexer: workspace must be 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t ld = round_up(T, 8);
+  if (int rc = indexer_scores_impl(q, k, k_batch_rows, w, freqs, B, S, H, D, T, rope_dim, pos0,
+                                   causal, ratio, workspace, ld, st))
+    return rc;
+  return topk_impl(workspace, ld, B, S, T, pos0, causal, ratio, topk, offset, out, out_dtype, st);
+}
+
+int ks_sparse_attn(const void* q, const void* kv, const float* attn_sink,
+                   const int32_t* topk_idxs, void* out, int64_t B, int64_t M, int64_t H,
+                   int64_t D, int64_t N, int64_t K, int64_t dv_begin, int64_t dv,
+                   float softmax_scale, void* stream) {
+  return sparse_attn_launch(q, kv, attn_sink, topk_idxs, out, B, M, H, D, N, K, dv_begin, dv,
+                            softmax_scale, static_cast<cudaStream_t>(stream));
+}
+
+int ks_device_status(void* stream) {
+  Device* dev;
+  if (int rc = device(&dev)) return rc;
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  int v = 0;
+  e = cudaMemcpy(&v, dev->status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read status word");
+  if (v != 0) {
+    const int zero = 0;
+    e = cudaMemcpy(dev->status, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "clear status word");
+    return fail(KS_ERR_DEVICE, "device status %d (%s)", v,
+                v == DEV_TIMEOUT ? "a bounded wait timed out" : "bounds check failed");
+  }
+  return KS_OK;
+}
+
+int ks_selftest_wait_timeout(uint64_t budget_ns, void* stream) {
+  Device* dev;
+  if (int rc = device(&dev)) return rc;
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(dev->status, budget_ns);
+  return launch_check("selftest_wait_kernel launch");
+}
+
+}  // extern "C"

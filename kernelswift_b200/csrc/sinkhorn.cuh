@@ -1,0 +1,182 @@
+// Sinkhorn normalisation of a batch of n x n fp32 matrices, all iterations on chip.
+//
+// Semantics follow baseline/sinkhorn.py:13-19 of KernelSwift:
+//   x = softmax(x, -1) + eps            (eps outside the softmax denominator)
+//   x = x / (colsum(x) + eps)
+//   repeat-1 times: x = x / (rowsum(x) + eps); x = x / (colsum(x) + eps)
+// One HBM read and one HBM write per matrix.  The reference NPU kernel
+// (optimized/sinkhorn_project/op_kernel/sinkhorn_kernel.asc:168-189) is limited
+// to 4x4; here any n is accepted.
+//
+// Register path (n <= 8): one thread owns one matrix in registers.  A block of
+// 128 threads stages its 128 contiguous matrices through shared memory so the
+// HBM traffic is 128-bit coalesced; the per-thread copy uses an odd word stride
+// (n*n + 1) so shared-memory reads are free of bank conflicts.
+// Warp path (8 < n <= 64): one warp per matrix in shared memory.
+#pragma once
+#include "ks_device.cuh"
+
+namespace ks {
+
+constexpr int SK_THREADS = 128;
+
+// 1/d, correctly rounded (used once per row or column per normalisation).
+__device__ __forceinline__ float sk_rcp(float d) { return __frcp_rn(d); }
+
+template <int N>
+__global__ void __launch_bounds__(SK_THREADS)
+    sinkhorn_reg_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t n_mats,
+                        int repeat, float eps) {
+  constexpr int NN = N * N;
+  constexpr int STRIDE = NN + 1;  // odd word stride: conflict-free per-thread access
+  extern __shared__ float sk_smem[];
+  const int tid = threadIdx.x;
+  const int64_t mat0 = (int64_t)blockIdx.x * SK_THREADS;
+  const int nm = (int)min((int64_t)SK_THREADS, n_mats - mat0);
+  const float* src = x + mat0 * NN;
+  float* dst = out + mat0 * NN;
+  const int total = nm * NN;
+
+  // coalesced load of the block's contiguous chunk into the padded layout
+  if (nm == SK_THREADS && (NN % 4) == 0) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    for (int v = tid; v < total / 4; v += SK_THREADS) {
+      float4 f = __ldcs(s4 + v);
+      int e = v * 4;
+      int m = e / NN, o = e % NN;
+      float* d = sk_smem + m * STRIDE + o;
+      d[0] = f.x; d[1] = f.y; d[2] = f.z; d[3] = f.w;
+    }
+  } else {
+    for (int e = tid; e < total; e += SK_THREADS) {
+      int m = e / NN, o = e % NN;
+      sk_smem[m * STRIDE + o] = __ldcs(src + e);
+    }
+  }
+  __syncthreads();
+
+  if (tid < nm) {
+    float a[N][N];
+    const float* my = sk_smem + tid * STRIDE;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < N; ++j) a[i][j] = my[i * N + j];
+
+    // softmax over the last dim, then + eps
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      float m = a[i][0];
+#pragma unroll
+      for (int j = 1; j < N; ++j) m = fmaxf(m, a[i][j]);
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        a[i][j] = expf(a[i][j] - m);
+        s += a[i][j];
+      }
+      const float r = sk_rcp(s);
+#pragma unroll
+      for (int j = 0; j < N; ++j) a[i][j] = a[i][j] * r + eps;
+    }
+    // baseline/sinkhorn.py:15-18: one column pass, then repeat-1 (row, column) pairs
+    const int rounds = repeat < 1 ? 1 : repeat;
+    for (int it = 0; it < rounds; ++it) {
+      if (it > 0) {  // row normalisation (skipped in the first round)
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          float s = 0.f;
+#pragma unroll
+          for (int j = 0; j < N; ++j) s += a[i][j];
+          const float r = sk_rcp(s + eps);
+#pragma unroll
+          for (int j = 0; j < N; ++j) a[i][j] *= r;
+        }
+      }
+      // column normalisation
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < N; ++i) s += a[i][j];
+        const float r = sk_rcp(s + eps);
+#pragma unroll
+        for (int i = 0; i < N; ++i) a[i][j] *= r;
+      }
+    }
+    float* myw = sk_smem + tid * STRIDE;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+#pragma unroll
+      for (int j = 0; j < N; ++j) myw[i * N + j] = a[i][j];
+  }
+  __syncthreads();
+
+  if (nm == SK_THREADS && (NN % 4) == 0) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    for (int v = tid; v < total / 4; v += SK_THREADS) {
+      int e = v * 4;
+      int m = e / NN, o = e % NN;
+      const float* s = sk_smem + m * STRIDE + o;
+      __stcs(d4 + v, make_float4(s[0], s[1], s[2], s[3]));
+    }
+  } else {
+    for (int e = tid; e < total; e += SK_THREADS) {
+      int m = e / NN, o = e % NN;
+      __stcs(dst + e, sk_smem[m * STRIDE + o]);
+    }
+  }
+}
+
+// One warp per matrix, matrix in shared memory with row stride n+1.
+constexpr int SKW_WARPS = 4;
+__global__ void __launch_bounds__(SKW_WARPS * 32)
+    sinkhorn_warp_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t n_mats,
+                         int n, int repeat, float eps) {
+  extern __shared__ float skw_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ld = n + 1;
+  float* a = skw_smem + warp * n * ld;
+  const int64_t mat = (int64_t)blockIdx.x * SKW_WARPS + warp;
+  if (mat >= n_mats) return;
+  const float* src = x + mat * n * n;
+  float* dst = out + mat * n * n;
+  for (int e = lane; e < n * n; e += 32) a[(e / n) * ld + e % n] = src[e];
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) {
+    float* row = a + i * ld;
+    float m = row[0];
+    for (int j = 1; j < n; ++j) m = fmaxf(m, row[j]);
+    float s = 0.f;
+    for (int j = 0; j < n; ++j) {
+      row[j] = expf(row[j] - m);
+      s += row[j];
+    }
+    const float r = sk_rcp(s);
+    for (int j = 0; j < n; ++j) row[j] = row[j] * r + eps;
+  }
+  __syncwarp();
+  const int rounds = repeat < 1 ? 1 : repeat;
+  for (int it = 0; it < rounds; ++it) {
+    if (it > 0) {
+      for (int i = lane; i < n; i += 32) {
+        float* row = a + i * ld;
+        float s = 0.f;
+        for (int j = 0; j < n; ++j) s += row[j];
+        const float r = sk_rcp(s + eps);
+        for (int j = 0; j < n; ++j) row[j] *= r;
+      }
+      __syncwarp();
+    }
+    for (int j = lane; j < n; j += 32) {
+      float s = 0.f;
+      for (int i = 0; i < n; ++i) s += a[i * ld + j];
+      const float r = sk_rcp(s + eps);
+      for (int i = 0; i < n; ++i) a[i * ld + j] *= r;
+    }
+    __syncwarp();
+  }
+  for (int e = lane; e < n * n; e += 32) dst[e] = a[(e / n) * ld + e % n];
+}
+
+}  // namespace ks

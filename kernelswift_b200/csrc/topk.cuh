@@ -1,0 +1,281 @@
+// Exact per-row top-k over bf16 score rows with the indexer's post-processing.
+//
+// Semantics follow baseline/indexer.py:185-205 of KernelSwift:
+//   * causal prefill rows only have keys t < (s+1)//ratio; the rest are -inf;
+//   * idx = topk(score, min(k, T)) sorted by value descending, ties by lower
+//     index (the order torch.topk returns on CUDA);
+//   * causal: idx >= (s+1)//ratio -> -1, else idx + offset; otherwise idx + offset.
+// The reference NPU kernel (optimized/indexer_project/op_kernel/indexer_topk.asc:
+// 155-248) is limited to k = 128 over 672 columns; here k <= 4096, T <= 65536.
+//
+// One CTA per row.  The valid prefix of the row is staged once in shared memory
+// as 16-bit order keys (monotone in the bf16 value, -0.0 folded onto +0.0).
+//   1. histogram of the high key byte (warp-aggregated shared atomics) and a
+//      suffix scan find the byte of the k-th largest key; a second histogram over
+//      the low byte of that bucket gives the exact threshold key `thr`, the count
+//      of keys above it and how many keys equal to it are taken (lowest indices
+//      first);
+//   2. one pass in index order compacts the selected (key, index) pairs with two
+//      block-wide exclusive scans per 4096-element chunk;
+//   3. a bitonic sort of the 32-bit composites ((0xFFFF-key)<<16 | index) puts
+//      them in (value desc, index asc) order; the composites are all distinct;
+//   4. the post-processed indices are written as int64 or int32.
+#pragma once
+#include "ks_device.cuh"
+
+namespace ks {
+
+constexpr int TK_THREADS = 512;
+constexpr int TK_WARPS = TK_THREADS / 32;
+constexpr int TK_PER_THREAD = 8;
+constexpr int TK_CHUNK = TK_THREADS * TK_PER_THREAD;
+
+struct TopkParams {
+  const uint16_t* scores;  // bf16 bits, row r at scores + r * row_stride
+  int64_t row_stride;      // elements, multiple of 8
+  int64_t rows;            // B * S
+  int64_t S;               // rows per batch
+  int64_t pos0;            // sequence position of row s = 0 (for the causal limit)
+  int32_t causal, ratio, T, k;  // k = number of outputs per row = min(topk, T)
+  int64_t offset;
+  void* out;               // [rows, k] int64 or int32
+  int32_t out_i64;
+  int64_t out_row_stride;  // elements
+  int32_t kpow2;           // power of two >= k
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t bf16_key(uint32_t u) {
+  u &= 0xFFFFu;
+  if (u == 0x8000u) u = 0;  // -0.0 == +0.0
+  return (u & 0x8000u) ? ((~u) & 0xFFFFu) : (u | 0x8000u);
+}
+
+__device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool pred) {
+  const uint32_t active = __ballot_sync(0xFFFFFFFFu, pred);
+  if (pred) {
+    const uint32_t peers = __match_any_sync(active, bin);
+    if ((threadIdx.x & 31) == (uint32_t)(__ffs(peers) - 1)) atomicAdd(hist + bin, __popc(peers));
+  }
+}
+
+// Exclusive scan of one value per thread over the block; also returns the total.
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* warp_tot,
+                                                    uint32_t& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += t;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < TK_WARPS ? warp_tot[lane] : 0;
+    uint32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      uint32_t t = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    if (lane < TK_WARPS) warp_tot[lane] = wi - w;  // exclusive warp offsets
+    if (lane == TK_WARPS - 1) warp_tot[TK_WARPS] = wi;
+  }
+  __syncthreads();
+  const uint32_t res = warp_tot[warp] + inc - v;
+  total = warp_tot[TK_WARPS];
+  __syncthreads();
+  return res;
+}
+
+// Given a 256-bin histogram, find the bin holding the `need`-th largest element.
+// Writes (bin, count strictly above the bin) to out2.  Uses the first 256 threads.
+__device__ __forceinline__ void find_bin(const uint32_t* hist, uint32_t need, uint32_t* scan,
+                                         uint32_t* out2) {
+  const int t = threadIdx.x;
+  if (t < 256) scan[t] = hist[255 - t];  // descending bin order
+  __syncthreads();
+  for (int o = 1; o < 256; o <<= 1) {
+    uint32_t v = 0;
+    if (t < 256 && t >= o) v = scan[t - o];
+    __syncthreads();
+    if (t < 256) scan[t] += v;
+    __syncthreads();
+  }
+  if (t < 256) {
+    const uint32_t incl = scan[t];
+    const uint32_t excl = t ? scan[t - 1] : 0;
+    if (incl >= need && excl < need) {
+      out2[0] = 255 - t;
+      out2[1] = excl;
+    }
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
+  extern __shared__ __align__(16) uint8_t tk_smem[];
+  // layout: sortbuf[kpow2] u32 | hist[256] | scan[256] | warp_tot[TK_WARPS+1] | misc[8] | keys
+  uint32_t* sortbuf = reinterpret_cast<uint32_t*>(tk_smem);
+  uint32_t* hist = sortbuf + p.kpow2;
+  uint32_t* scan = hist + 256;
+  uint32_t* warp_tot = scan + 256;
+  uint32_t* misc = warp_tot + TK_WARPS + 4;
+  uint16_t* keys = reinterpret_cast<uint16_t*>(misc + 8);
+
+  const int tid = threadIdx.x;
+  const int64_t row = p.rows - 1 - (int64_t)blockIdx.x;  // longest causal rows first
+  const int64_t s = row % p.S;
+  int64_t lim64 = p.causal ? (p.pos0 + s + 1) / p.ratio : (int64_t)p.T;
+  if (lim64 > p.T) lim64 = p.T;
+  if (lim64 < 0) lim64 = 0;
+  const int L = (int)lim64;
+  const int K = p.k;
+  const uint16_t* src = p.scores + row * p.row_stride;
+
+  if (tid < 256) hist[tid] = 0;
+  __syncthreads();
+
+  // ---- stage the valid prefix as order keys, histogram of the high byte
+  const bool need_select = L > K;
+  for (int base = 0; base < L; base += TK_CHUNK) {
+    const int i0 = base + tid * TK_PER_THREAD;
+    uint32_t kv[TK_PER_THREAD];
+    if (i0 + TK_PER_THREAD <= L) {
+      const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src + i0));
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        kv[2 * q] = bf16_key(w[q] & 0xFFFFu);
+        kv[2 * q + 1] = bf16_key(w[q] >> 16);
+      }
+      uint4 o;
+      o.x = kv[0] | (kv[1] << 16);
+      o.y = kv[2] | (kv[3] << 16);
+      o.z = kv[4] | (kv[5] << 16);
+      o.w = kv[6] | (kv[7] << 16);
+      *reinterpret_cast<uint4*>(keys + i0) = o;
+    } else {
+#pragma unroll
+      for (int q = 0; q < TK_PER_THREAD; ++q) {
+        kv[q] = 0;
+        if (i0 + q < L) {
+          kv[q] = bf16_key(src[i0 + q]);
+          keys[i0 + q] = (uint16_t)kv[q];
+        }
+      }
+    }
+    if (need_select) {
+#pragma unroll
+      for (int q = 0; q < TK_PER_THREAD; ++q) hist_add(hist, kv[q] >> 8, i0 + q < L);
+    }
+  }
+  __syncthreads();
+
+  uint32_t thr = 0, need_eq = 0;
+  if (need_select) {
+    find_bin(hist, (uint32_t)K, scan, misc);
+    const uint32_t b1 = misc[0], above1 = misc[1];
+    if (tid < 256) hist[tid] = 0;
+    __syncthreads();
+    for (int base = 0; base < L; base += TK_CHUNK) {
+      const int i0 = base + tid * TK_PER_THREAD;
+#pragma unroll
+      for (int q = 0; q < TK_PER_THREAD; ++q) {
+        const bool in = i0 + q < L;
+        const uint32_t key = in ? keys[i0 + q] : 0u;
+        hist_add(hist, key & 0xFFu, in && (key >> 8) == b1);
+      }
+    }
+    __syncthreads();
+    find_bin(hist, (uint32_t)K - above1, scan, misc + 2);
+    const uint32_t b2 = misc[2], above2 = misc[3];
+    thr = (b1 << 8) | b2;
+    need_eq = (uint32_t)K - above1 - above2;
+  }
+
+  // ---- compaction in index order
+  const int nsel = need_select ? K : L;
+  uint32_t eq_base = 0, sel_base = 0;
+  for (int base = 0; base < L; base += TK_CHUNK) {
+    const int i0 = base + tid * TK_PER_THREAD;
+    uint32_t kq[TK_PER_THREAD];
+    uint32_t n_eq = 0;
+#pragma unroll
+    for (int q = 0; q < TK_PER_THREAD; ++q) {
+      kq[q] = (i0 + q < L) ? keys[i0 + q] : 0u;
+      n_eq += (i0 + q < L && kq[q] == thr) ? 1u : 0u;
+    }
+    uint32_t eq_tot;
+    const uint32_t eq_pre = need_select ? block_excl_scan(n_eq, warp_tot, eq_tot) : 0u;
+    uint32_t n_sel = 0;
+    uint32_t r = eq_base + eq_pre;
+    uint32_t selmask = 0;
+#pragma unroll
+    for (int q = 0; q < TK_PER_THREAD; ++q) {
+      bool sel = false;
+      if (i0 + q < L) {
+        if (!need_select || kq[q] > thr) {
+          sel = true;
+        } else if (kq[q] == thr) {
+          sel = r < need_eq;
+          ++r;
+        }
+      }
+      if (sel) {
+        selmask |= 1u << q;
+        ++n_sel;
+      }
+    }
+    uint32_t sel_tot;
+    uint32_t pos = sel_base + block_excl_scan(n_sel, warp_tot, sel_tot);
+#pragma unroll
+    for (int q = 0; q < TK_PER_THREAD; ++q) {
+      if (selmask & (1u << q)) {
+        if (pos < (uint32_t)p.kpow2)
+          sortbuf[pos] = ((0xFFFFu - kq[q]) << 16) | (uint32_t)(i0 + q);
+        ++pos;
+      }
+    }
+    if (need_select) eq_base += eq_tot;
+    sel_base += sel_tot;
+  }
+  // pad to the power of two
+  for (int i = nsel + tid; i < p.kpow2; i += TK_THREADS) sortbuf[i] = 0xFFFFFFFFu;
+  __syncthreads();
+
+  // ---- bitonic sort, ascending composites
+  const int n = p.kpow2;
+  for (int kk = 2; kk <= n; kk <<= 1) {
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < n; i += TK_THREADS) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint32_t a = sortbuf[i], b = sortbuf[ixj];
+          const bool up = (i & kk) == 0;
+          if ((a > b) == up) {
+            sortbuf[i] = b;
+            sortbuf[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+
+  // ---- post-process and write
+  for (int i = tid; i < K; i += TK_THREADS) {
+    int64_t o = -1;
+    if (i < nsel) {
+      const int64_t idx = (int64_t)(sortbuf[i] & 0xFFFFu);
+      o = (p.causal && idx >= lim64) ? -1 : idx + p.offset;
+    }
+    if (p.out_i64)
+      reinterpret_cast<int64_t*>(p.out)[row * p.out_row_stride + i] = o;
+    else
+      reinterpret_cast<int32_t*>(p.out)[row * p.out_row_stride + i] = (int32_t)o;
+  }
+}
+
+}  // namespace ks

@@ -1,0 +1,194 @@
+"""torch-facing operators over the C ABI of libks_b200.so.
+
+These are the B200 counterparts of the reference's torch extension ops
+(KernelSwift ``optimized/*/op_extension``):
+
+* ``sinkhorn``        <- ``sinkhorn_ext.sinkhorn`` (sinkhorn_torch.cpp:18-66)
+* ``sparse_attn``     <- ``torch.ops.npu.sparse_attn_megakernel_basic`` (sparse_attn_torch.cpp:96-160)
+* ``indexer_topk``    <- ``indexer_ops.rope_inplace`` + ``fused_qk_reduce`` + ``topk_mask``
+  (indexer_torch.cpp:100-268), fused behind one call
+* ``indexer_scores`` / ``topk_rows`` expose the two indexer stages separately.
+
+Every op runs on the current CUDA stream of its input's device, validates its
+arguments like the reference (a ``RuntimeError`` on a bad dtype, device, shape
+or layout) and has no CPU fallback.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._lib import KS_INT32, KS_INT64, check, lib
+
+_DV_MAX = 512
+
+
+def _require_cuda(name: str, *tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+            raise RuntimeError(f"{name}: inputs must be CUDA tensors")
+        if not t.is_contiguous():
+            raise RuntimeError(f"{name}: inputs must be contiguous")
+    dev = tensors[0].device
+    if any(t.device != dev for t in tensors):
+        raise RuntimeError(f"{name}: inputs must be on one device")
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def sinkhorn(x: torch.Tensor, repeat: int = 10, eps: float = 1e-6,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """Sinkhorn normalisation over the last two dims of ``x`` ([..., n, n] fp32)."""
+    if x.dtype != torch.float32:
+        raise RuntimeError("sinkhorn: x must be float32")
+    if x.dim() < 2 or x.shape[-1] != x.shape[-2]:
+        raise RuntimeError("sinkhorn: x must be [..., n, n]")
+    _require_cuda("sinkhorn", x)
+    out = torch.empty_like(x) if out is None else out
+    n = x.shape[-1]
+    n_mats = x.numel() // (n * n) if n else 0
+    with torch.cuda.device(x.device):
+        check(lib().ks_sinkhorn(_ptr(x), _ptr(out), n_mats, n, int(repeat), float(eps),
+                                _stream(x)), "ks_sinkhorn")
+    return out
+
+
+def sparse_attn(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor,
+                topk_idxs: torch.Tensor, softmax_scale: float, dv: int | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Top-k gathered MQA attention with a per-head sink (baseline/sparse_attention.py:5-42).
+
+    q bf16 [B,M,H,D], kv bf16 [B,N,D], attn_sink fp32 [H], topk_idxs int32 [B,M,K].
+    Returns bf16 [B,M,H,dv] = the first ``dv`` (default D) output columns."""
+    if q.dtype != torch.bfloat16 or kv.dtype != torch.bfloat16:
+        raise RuntimeError("sparse_attn: q and kv must be bfloat16")
+    if attn_sink.dtype != torch.float32:
+        raise RuntimeError("sparse_attn: attn_sink must be float32")
+    if topk_idxs.dtype != torch.int32:
+        raise RuntimeError("sparse_attn: topk_idxs must be int32")
+    if q.dim() != 4 or kv.dim() != 3 or attn_sink.dim() != 1 or topk_idxs.dim() != 3:
+        raise RuntimeError("sparse_attn: expected q [b,m,h,d], kv [b,n,d], sink [h], idx [b,m,k]")
+    B, M, H, D = q.shape
+    N, K = kv.shape[1], topk_idxs.shape[2]
+    if kv.shape[0] != B or kv.shape[2] != D:
+        raise RuntimeError("sparse_attn: kv shape mismatch")
+    if attn_sink.shape[0] != H:
+        raise RuntimeError("sparse_attn: attn_sink shape mismatch")
+    if topk_idxs.shape[0] != B or topk_idxs.shape[1] != M:
+        raise RuntimeError("sparse_attn: topk_idxs shape mismatch")
+    _require_cuda("sparse_attn", q, kv, attn_sink, topk_idxs)
+    dv = D if dv is None else int(dv)
+    if out is None:
+        out = torch.empty((B, M, H, dv), dtype=torch.bfloat16, device=q.device)
+    with torch.cuda.device(q.device):
+        if dv <= _DV_MAX:
+            check(lib().ks_sparse_attn(_ptr(q), _ptr(kv), _ptr(attn_sink), _ptr(topk_idxs),
+                                       _ptr(out), B, M, H, D, N, K, 0, dv, float(softmax_scale),
+                                       _stream(q)), "ks_sparse_attn")
+        else:  # output wider than one pass: column slices, each a full kernel call
+            for c0 in range(0, dv, _DV_MAX):
+                c1 = min(dv, c0 + _DV_MAX)
+                part = torch.empty((B, M, H, c1 - c0), dtype=torch.bfloat16, device=q.device)
+                check(lib().ks_sparse_attn(_ptr(q), _ptr(kv), _ptr(attn_sink), _ptr(topk_idxs),
+                                           _ptr(part), B, M, H, D, N, K, c0, c1 - c0,
+                                           float(softmax_scale), _stream(q)), "ks_sparse_attn")
+                out[..., c0:c1].copy_(part)
+    return out
+
+
+def _indexer_args(q, k, w, freqs, T):
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise RuntimeError("indexer: q, k and w must be bfloat16")
+    if freqs is not None and freqs.dtype != torch.float32:
+        raise RuntimeError("indexer: freqs must be float32 [s, rope_dim/2, 2]")
+    if q.dim() != 4 or k.dim() != 3 or w.dim() != 3:
+        raise RuntimeError("indexer: expected q [b,s,h,d], k [b,t,d], w [b,s,h]")
+    B, S, H, D = q.shape
+    if k.shape[0] < B or k.shape[2] != D or k.shape[1] < T:
+        raise RuntimeError("indexer: k shape mismatch")
+    if tuple(w.shape) != (B, S, H):
+        raise RuntimeError("indexer: w shape mismatch")
+    ts = [q, k[:B], w] + ([freqs] if freqs is not None else [])
+    _require_cuda("indexer", *ts)
+    return B, S, H, D
+
+
+def indexer_workspace_size(B: int, S: int, T: int) -> int:
+    return int(lib().ks_indexer_workspace_size(B, S, T))
+
+
+def indexer_topk(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, freqs: torch.Tensor | None,
+                 rope_dim: int, T: int, topk: int, ratio: int = 1, causal: bool = True,
+                 offset: int = 0, pos0: int = 0, out_dtype: torch.dtype = torch.int64,
+                 out: torch.Tensor | None = None,
+                 workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Indexer top-k after the projections (baseline/indexer.py:170-205).
+
+    q bf16 [B,S,H,D] before RoPE, k bf16 [B,Tk>=T,D] (rows t < T used), w bf16
+    [B,S,H], freqs fp32 [S, rope_dim/2, 2].  Returns [B,S,min(topk,T)]."""
+    B, S, H, D = _indexer_args(q, k, w, freqs, T)
+    kk = min(int(topk), int(T))
+    if out is None:
+        out = torch.empty((B, S, kk), dtype=out_dtype, device=q.device)
+    if T == 0:
+        return out
+    need = indexer_workspace_size(B, S, T)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        check(lib().ks_indexer(_ptr(q), _ptr(k), k.shape[1], _ptr(w), _ptr(freqs), B, S, H, D,
+                               int(T), int(rope_dim), int(pos0), int(bool(causal)), int(ratio),
+                               int(topk), int(offset), _ptr(out),
+                               KS_INT64 if out.dtype == torch.int64 else KS_INT32,
+                               _ptr(workspace), workspace.numel(), _stream(q)), "ks_indexer")
+    return out
+
+
+def indexer_scores(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, freqs: torch.Tensor | None,
+                   rope_dim: int, T: int, ratio: int = 1, causal: bool = True,
+                   pos0: int = 0) -> torch.Tensor:
+    """Score stage alone: bf16 [B, S, ld] (ld = T rounded up to 8); columns at or
+    beyond a row's causal limit are -inf inside the last 128-key tile and
+    unwritten after it."""
+    B, S, H, D = _indexer_args(q, k, w, freqs, T)
+    ld = (int(T) + 7) // 8 * 8
+    scores = torch.full((B, S, ld), float("-inf"), dtype=torch.bfloat16, device=q.device)
+    with torch.cuda.device(q.device):
+        check(lib().ks_indexer_scores(_ptr(q), _ptr(k), k.shape[1], _ptr(w), _ptr(freqs), B, S,
+                                      H, D, int(T), int(rope_dim), int(pos0), int(bool(causal)),
+                                      int(ratio), _ptr(scores), ld, _stream(q)),
+              "ks_indexer_scores")
+    return scores
+
+
+def topk_rows(scores: torch.Tensor, T: int, topk: int, ratio: int = 1, causal: bool = True,
+              offset: int = 0, pos0: int = 0, out_dtype: torch.dtype = torch.int64
+              ) -> torch.Tensor:
+    """Top-k stage alone over bf16 scores [B, S, ld>=T] (ld % 8 == 0)."""
+    if scores.dtype != torch.bfloat16 or scores.dim() != 3:
+        raise RuntimeError("topk_rows: scores must be bf16 [b, s, ld]")
+    _require_cuda("topk_rows", scores)
+    B, S, ld = scores.shape
+    kk = min(int(topk), int(T))
+    out = torch.empty((B, S, kk), dtype=out_dtype, device=scores.device)
+    with torch.cuda.device(scores.device):
+        check(lib().ks_topk_rows(_ptr(scores), ld, B, S, int(T), int(pos0), int(bool(causal)),
+                                 int(ratio), int(topk), int(offset), _ptr(out),
+                                 KS_INT64 if out_dtype == torch.int64 else KS_INT32,
+                                 _stream(scores)), "ks_topk_rows")
+    return out
+
+
+def device_status(device: torch.device | int | None = None) -> None:
+    """Synchronise the current stream and raise if a kernel reported a timed-out
+    wait or a bounds error since the last check."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index or 0))
+    with torch.cuda.device(dev):
+        check(lib().ks_device_status(torch.cuda.current_stream(dev).cuda_stream),
+              "ks_device_status")
