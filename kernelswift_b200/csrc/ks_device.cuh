@@ -9,7 +9,8 @@
 //  * UMMA shared-memory / instruction descriptors for the 128-byte-swizzled
 //    canonical layouts that TMA writes.
 //
-// No TMA load in this library uses cluster multicast.
+// Every TMA load here writes only the issuing CTA's own shared memory and reads
+// only this GPU's global memory.
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -119,6 +120,18 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const Wai
       }
     }
   }
+}
+
+// ------------------------------------------------------------------ clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of every CTA in the cluster.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
 }
 
 // ------------------------------------------------------------------ proxies / fences

@@ -48,8 +48,9 @@ def check(q_pre, kv, w, freqs, rd, k, ratio, start_pos, offset, pos0=0, max_flip
     ref_sc = O.indexer_scores(O.rope_last(q_pre, freqs, rd), kv, w, causal, ratio, pos0)
     flips = (sc != ref_sc) & valid
     assert flips.mean() <= max_flip, f"score flips {flips.mean():.2e}"
-    dist = np.abs(O.bf16_order_key(sc).astype(np.int64) - O.bf16_order_key(ref_sc).astype(np.int64))
-    assert dist[valid].max(initial=0) <= 16
+    # a flip moves a score by about one bf16 ulp of one head's product: small in absolute terms
+    a, r = O.bf16_to_f32(sc)[valid], O.bf16_to_f32(ref_sc)[valid]
+    assert np.allclose(a, r, rtol=1e-2, atol=1e-2)
     # top-k exact on the kernel's own scores
     own = sc.copy()
     own[~valid] = O.NEG_INF_BF16
