@@ -251,6 +251,66 @@ int topk_impl(const void* scores, int64_t score_ld, int64_t B, int64_t S, int64_
   return launch_check("topk_rows_kernel launch");
 }
 
+int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int32_t* idx,
+                     void* out, int64_t B, int64_t M, int64_t H, int64_t D, int64_t N, int64_t K,
+                     int64_t dv_begin, int64_t dv, float scale, cudaStream_t st) {
+  Device* dev;
+  if (int rc = device(&dev)) return rc;
+  if (!q || !kv || !sink || !idx || !out) return fail(KS_ERR_INVALID, "sparse_attn: null pointer");
+  if (B < 1 || M < 0 || H < 1 || N < 1 || K < 1) return fail(KS_ERR_INVALID, "sparse_attn: bad sizes");
+  if (H > 128) return fail(KS_ERR_UNSUPPORTED, "sparse_attn: H=%lld > 128", (long long)H);
+  if (D % 64 || D < 64 || D > 576) return fail(KS_ERR_UNSUPPORTED, "sparse_attn: D=%lld (multiple of 64, <= 576)", (long long)D);
+  if (dv < 64 || dv > 512 || dv % 64 || dv_begin < 0 || dv_begin % 64 || dv_begin + dv > D)
+    return fail(KS_ERR_UNSUPPORTED, "sparse_attn: dv=%lld dv_begin=%lld (multiples of 64, dv <= 512, within D)", (long long)dv, (long long)dv_begin);
+  if (!aligned(q, 16) || !aligned(kv, 16) || !aligned(out, 16) || !aligned(idx, 4) || !aligned(sink, 4))
+    return fail(KS_ERR_ALIGNMENT, "sparse_attn: q, kv, out must be 16-byte aligned");
+  if (B * M * H >= (1ll << 31) || B * N >= (1ll << 31) || 2 * B * M >= (1ll << 31))
+    return fail(KS_ERR_UNSUPPORTED, "sparse_attn: too many rows");
+  if (M == 0) return KS_OK;
+  SaParams p{};
+  p.idx = idx;
+  p.sink = sink;
+  p.out = static_cast<uint16_t*>(out);
+  p.B = (int)B; p.M = (int)M; p.H = (int)H; p.D = (int)D; p.N = (int)N; p.K = (int)K;
+  p.dv_begin = (int)dv_begin;
+  p.dv = (int)dv;
+  p.dv_pad = (int)round_up(dv, 128);
+  p.n_pv = (p.dv_pad + 255) / 256;
+  p.n_pvblk = 0;
+  for (int i = 0; i < p.n_pv; ++i) {
+    p.pv_n[i] = p.dv_pad - 256 * i < 256 ? p.dv_pad - 256 * i : 256;
+    p.n_pvblk += p.pv_n[i] / 128;
+  }
+  p.nblk = (int)((K + SA_NB - 1) / SA_NB);
+  const uint32_t nkb = (uint32_t)(D / 64);
+  p.q_off = SA_HDR;
+  p.p_off = p.q_off + nkb * 8192;
+  p.st_off = p.p_off + 8192;
+  p.sreg_bytes = nkb * 4096;
+  p.st_bytes = p.sreg_bytes + p.n_pvblk * 8192;
+  const size_t limit = 232448;
+  const size_t fixed = 1024 + p.st_off;
+  int nst = (int)((limit - fixed) / p.st_bytes);
+  if (nst > SA_MAX_ST) nst = SA_MAX_ST;
+  if (nst < 2) return fail(KS_ERR_UNSUPPORTED, "sparse_attn: shared memory too small for D=%lld dv=%lld", (long long)D, (long long)dv);
+  p.nst = nst;
+  const size_t smem = fixed + (size_t)nst * p.st_bytes;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.status = dev->status;
+  p.budget_ns = wait_budget_ns();
+  CUtensorMap qm, km;
+  if (int rc = make_map_bf16(&qm, q, D, (uint64_t)(B * M * H), D * 2, 64, 64)) return rc;
+  if (int rc = make_map_bf16(&km, kv, D, (uint64_t)(B * N), D * 2, 64, 1)) return rc;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(sparse_attn)");
+  sparse_attn_kernel<<<(unsigned)(2 * B * M), SA_THREADS, smem, st>>>(qm, km, p);
+  return launch_check("sparse_attn_kernel launch");
+}
+
 __global__ void selftest_wait_kernel(int* status, uint64_t budget_ns) {
   __shared__ uint64_t bar;
   __shared__ int abort_flag;
@@ -364,8 +424,8 @@ int ks_sparse_attn(const void* q, const void* kv, const float* attn_sink,
                    const int32_t* topk_idxs, void* out, int64_t B, int64_t M, int64_t H,
                    int64_t D, int64_t N, int64_t K, int64_t dv_begin, int64_t dv,
                    float softmax_scale, void* stream) {
-  return sparse_attn_launch(q, kv, attn_sink, topk_idxs, out, B, M, H, D, N, K, dv_begin, dv,
-                            softmax_scale, static_cast<cudaStream_t>(stream));
+  return sparse_attn_impl(q, kv, attn_sink, topk_idxs, out, B, M, H, D, N, K, dv_begin, dv,
+                          softmax_scale, static_cast<cudaStream_t>(stream));
 }
 
 int ks_device_status(void* stream) {

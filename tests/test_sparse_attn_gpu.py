@@ -1,0 +1,130 @@
+"""SparseAttention kernel vs the golden fixtures and the oracle
+(baseline/sparse_attention.py:5-42).  Float outputs: the harness tolerance
+atol = rtol = 1e-2, plus a tighter check on the mean error."""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, load_golden
+from helpers import bf16_from_bits, bits_from_bf16
+from oracle import ks_oracle as O
+
+SA = sorted(os.path.basename(f)[:-4] for f in glob.glob(os.path.join(GOLDEN, "sa_*.npz")))
+pytestmark = pytest.mark.gpu
+
+
+def assert_close(got_bits, ref_bits):
+    a = O.bf16_to_f32(got_bits).astype(np.float64)
+    r = O.bf16_to_f32(ref_bits).astype(np.float64)
+    assert np.all(np.isfinite(a))
+    assert np.allclose(a, r, atol=1e-2, rtol=1e-2), f"max abs diff {np.abs(a - r).max():.3e}"
+    assert np.abs(a - r).mean() < 2e-3
+
+
+@pytest.mark.parametrize("name", SA)
+def test_golden(cuda_ok, name):
+    from kernelswift_b200 import ops
+
+    d = load_golden(name)
+    out = ops.sparse_attn(bf16_from_bits(d["q"]), bf16_from_bits(d["kv"]),
+                          torch.from_numpy(d["sink"]).cuda(), torch.from_numpy(d["idx"]).cuda(),
+                          float(d["scale"]))
+    ops.device_status()
+    assert_close(bits_from_bf16(out), d["out"])
+
+
+def make_case(B, M, H, D, N, K, seed, mode="perm", sink="randn"):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, M, H, D, generator=g).bfloat16()
+    kv = torch.randn(B, N, D, generator=g).bfloat16()
+    if mode == "perm":
+        idx = torch.stack([torch.stack([torch.randperm(N, generator=g)[:K] for _ in range(M)])
+                           for _ in range(B)]).int()
+    else:
+        idx = torch.randint(-N // 4, N, (B, M, K), generator=g).int()  # duplicates and -1s
+        idx[idx < 0] = -1
+    s = torch.randn(H, generator=g) if sink == "randn" else torch.zeros(H)
+    return q, kv, s, idx
+
+
+CASES = [
+    # B, M, H, D, N, K, dv, mode
+    (1, 128, 16, 128, 4096, 512, 128, "perm"),     # C2
+    (2, 5, 128, 576, 2048, 512, 512, "perm"),      # MLA heads, dv = 512 of D = 576
+    (1, 7, 128, 576, 1000, 100, 512, "mixed"),     # ragged K, duplicates, -1
+    (1, 6, 64, 128, 32, 16, 128, "mixed"),         # reference geometry
+    (3, 3, 24, 192, 300, 130, 192, "perm"),        # odd H, dv not a multiple of 128
+    (1, 4, 128, 256, 777, 64, 64, "mixed"),        # dv = 64
+]
+
+
+@pytest.mark.parametrize("B,M,H,D,N,K,dv,mode", CASES)
+def test_vs_oracle(cuda_ok, B, M, H, D, N, K, dv, mode):
+    from kernelswift_b200 import ops
+
+    q, kv, s, idx = make_case(B, M, H, D, N, K, seed=B * 100 + M + H + K, mode=mode)
+    out = ops.sparse_attn(q.cuda(), kv.cuda(), s.cuda(), idx.cuda(), D ** -0.5, dv)
+    ops.device_status()
+    ref = O.sparse_attn(bits_from_bf16(q), bits_from_bf16(kv), s.numpy(), idx.numpy(), D ** -0.5, dv)
+    assert_close(bits_from_bf16(out), ref)
+
+
+def test_column_slice(cuda_ok):
+    """dv_begin > 0 (the second pass of a D = 576 output) equals those columns of a full call."""
+    from kernelswift_b200 import _lib, ops
+
+    B, M, H, D, N, K = 1, 3, 128, 576, 512, 128
+    q, kv, s, idx = make_case(B, M, H, D, N, K, seed=9)
+    q, kv, s, idx = q.cuda(), kv.cuda(), s.cuda(), idx.cuda()
+    full = ops.sparse_attn(q, kv, s, idx, D ** -0.5)  # 576 columns: 512 + 64
+    part = torch.empty(B, M, H, 64, dtype=torch.bfloat16, device="cuda")
+    _lib.check(_lib.lib().ks_sparse_attn(q.data_ptr(), kv.data_ptr(), s.data_ptr(), idx.data_ptr(),
+                                         part.data_ptr(), B, M, H, D, N, K, 512, 64, D ** -0.5,
+                                         torch.cuda.current_stream().cuda_stream), "sa")
+    ops.device_status()
+    assert torch.equal(full[..., 512:], part)
+    ref = O.sparse_attn(bits_from_bf16(q), bits_from_bf16(kv), s.cpu().numpy(), idx.cpu().numpy(), D ** -0.5)
+    assert_close(bits_from_bf16(full), ref)
+
+
+def test_edge_rows(cuda_ok):
+    """All-invalid rows give 0; a single repeated row gives that row; sinks weigh in."""
+    from kernelswift_b200 import ops
+
+    B, M, H, D, N, K = 1, 4, 16, 128, 64, 96
+    q, kv, s, idx = make_case(B, M, H, D, N, K, seed=3)
+    idx[0, 0] = -1
+    idx[0, 1] = 5
+    idx[0, 2, 1:] = -1
+    out = ops.sparse_attn(q.cuda(), kv.cuda(), torch.full((H,), -1e4).cuda(), idx.cuda(), D ** -0.5)
+    ops.device_status()
+    o = out.float().cpu()
+    assert torch.all(o[0, 0] == 0)
+    assert torch.allclose(o[0, 1], kv[0, 5].float().expand(H, D), atol=1e-2, rtol=1e-2)
+    assert torch.allclose(o[0, 2], kv[0, idx[0, 2, 0]].float().expand(H, D), atol=1e-2, rtol=1e-2)
+
+
+def test_mla_scale_rows(cuda_ok):
+    """C4 geometry (4, 4096, 128, 576), N = 32768, K = 2048, dv = 512, causal-valid
+    indices; the oracle checks a sample of rows."""
+    from kernelswift_b200 import ops
+
+    B, M, H, D, N, K, dv = 4, 4096, 128, 576, 32768, 2048, 512
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, M, H, D, device="cuda", generator=g).bfloat16()
+    kv = torch.randn(B, N, D, device="cuda", generator=g).bfloat16()
+    pos = N - M + torch.arange(M, device="cuda")
+    r = torch.rand(B, M, K, device="cuda", generator=g)
+    idx = (r * (pos[None, :, None] + 1).float()).long().clamp_max(N - 1).int()
+    sink = torch.zeros(H, device="cuda")
+    out = ops.sparse_attn(q, kv, sink, idx, D ** -0.5, dv)
+    ops.device_status()
+    rows = [0, 1, 2047, 4095]
+    for b in (0, 3):
+        qb = bits_from_bf16(q[b:b + 1, rows])
+        ib = idx[b:b + 1, rows].cpu().numpy()
+        ref = O.sparse_attn(qb, bits_from_bf16(kv[b:b + 1]), sink.cpu().numpy(), ib, D ** -0.5, dv)
+        assert_close(bits_from_bf16(out[b:b + 1, rows]), ref)
