@@ -269,6 +269,7 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
   if (M == 0) return KS_OK;
   SaParams p{};
   p.idx = idx;
+  p.kv = static_cast<const uint16_t*>(kv);
   p.sink = sink;
   p.out = static_cast<uint16_t*>(out);
   p.B = (int)B; p.M = (int)M; p.H = (int)H; p.D = (int)D; p.N = (int)N; p.K = (int)K;
@@ -279,13 +280,18 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
   p.n_pvblk = 0;
   for (int i = 0; i < p.n_pv; ++i) {
     p.pv_n[i] = p.dv_pad - 256 * i < 256 ? p.dv_pad - 256 * i : 256;
+    // CTA c supplies columns [256 i + c * n/2, 256 i + (c + 1) * n/2) of instruction i
+    for (int c = 0; c < 2; ++c)
+      for (int v = 0; v < p.pv_n[i] / 128; ++v)
+        p.pv_col[c][p.n_pvblk + v] = 256 * i + c * (p.pv_n[i] / 2) + 64 * v;
     p.n_pvblk += p.pv_n[i] / 128;
   }
   p.nblk = (int)((K + SA_NB - 1) / SA_NB);
+  p.idx_vec4 = (K % 4 == 0) && aligned(idx, 16);
   const uint32_t nkb = (uint32_t)(D / 64);
   p.q_off = SA_HDR;
   p.p_off = p.q_off + nkb * 8192;
-  p.st_off = p.p_off + 8192;
+  p.st_off = p.p_off + 2 * 8192;  // P double buffered
   p.sreg_bytes = nkb * 4096;
   p.st_bytes = p.sreg_bytes + p.n_pvblk * 8192;
   const size_t limit = 232448;
@@ -298,16 +304,15 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = dev->status;
   p.budget_ns = wait_budget_ns();
-  CUtensorMap qm, km;
+  CUtensorMap qm;
   if (int rc = make_map_bf16(&qm, q, D, (uint64_t)(B * M * H), D * 2, 64, 64)) return rc;
-  if (int rc = make_map_bf16(&km, kv, D, (uint64_t)(B * N), D * 2, 64, 1)) return rc;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
     attr_err = cudaFuncSetAttribute(sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(sparse_attn)");
-  sparse_attn_kernel<<<(unsigned)(2 * B * M), SA_THREADS, smem, st>>>(qm, km, p);
+  sparse_attn_kernel<<<(unsigned)(2 * B * M), SA_THREADS, smem, st>>>(qm, p);
   return launch_check("sparse_attn_kernel launch");
 }
 

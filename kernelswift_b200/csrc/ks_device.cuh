@@ -87,6 +87,28 @@ __device__ __forceinline__ bool mbar_test_cluster(uint32_t bar, uint32_t parity)
   return ok != 0;
 }
 
+// Non-blocking probes (mbarrier.test_wait): for loops that poll several barriers;
+// try_wait may suspend the thread on the first incomplete barrier it probes.
+__device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_poll_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;"
+      " selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Shared state every bounded wait consults: the CTA-local abort flag (in shared
 // memory), the global status word and the time budget of one wait.
 struct WaitCtx {
@@ -94,6 +116,12 @@ struct WaitCtx {
   int* status;          // global memory, may be null
   uint64_t budget_ns;
 };
+
+// Budgets are enforced with the SM cycle counter (cheap to read, unlike
+// %globaltimer): at most 2 cycles per ns below 2 GHz, so a budget of B ns
+// expires after at most 2B cycles, i.e. between B/2 and 2B ns of wall time for
+// SM clocks from 1 to 2 GHz.
+__device__ __forceinline__ uint64_t budget_cycles(uint64_t budget_ns) { return budget_ns * 2; }
 
 __device__ __forceinline__ void raise_error(const WaitCtx& w, int code) {
   *w.abort = 1;
@@ -109,12 +137,13 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const Wai
                                        bool cluster_scope = false, bool drain = false) {
   const uint32_t b = smem_u32(bar);
   if (cluster_scope ? mbar_test_cluster(b, parity) : mbar_test(b, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const uint64_t t0 = clock64();
+  const uint64_t lim = budget_cycles(w.budget_ns);
   for (uint32_t it = 1;; ++it) {
     if (cluster_scope ? mbar_test_cluster(b, parity) : mbar_test(b, parity)) return true;
     if ((it & 15) == 0) {
       if (!drain && *w.abort) return false;
-      if (globaltimer_ns() - t0 > w.budget_ns) {
+      if ((uint64_t)clock64() - t0 > lim) {
         raise_error(w, DEV_TIMEOUT);
         return false;
       }
@@ -168,6 +197,23 @@ __device__ __forceinline__ void tma_gather4(const CUtensorMap* m, uint64_t* bar,
       "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2),
       "r"(y3)
       : "memory");
+}
+
+// ------------------------------------------------------------------ cp.async (16 bytes)
+// Copy 16 bytes global -> shared (L2 only); src_bytes < 16 zero-fills the rest.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes = 16) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+// Arrive on `bar` once every cp.async this thread issued so far has landed (the
+// arrival counts against the barrier's expected count).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // ------------------------------------------------------------------ tcgen05

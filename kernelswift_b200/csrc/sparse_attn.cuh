@@ -19,14 +19,16 @@
 //   PV:  O[64 heads, dv] per CTA += P[64, 64 keys] . V[64 keys, dv]; each CTA
 //        supplies its half of every PV instruction's N columns, for all 64 keys
 //        (so its V rows include the peer's keys in those columns).
-// Rows are gathered from HBM/L2 with TMA tile::gather4 (4 rows x 128 bytes per
-// instruction) into the 128-byte-swizzled layout; the same rows serve as the
-// K-major B operand of QK and the MN-major B operand of PV.
+// Rows are gathered with 16-byte cp.async copies (the swizzle computed per copy)
+// into the 128-byte-swizzled layout; the same rows serve as the K-major B
+// operand of QK and the MN-major B operand of PV.  (TMA tile::gather4 moves only
+// four 128-byte rows per instruction; issuing the ~136 instructions a block needs
+// took ~5 us per block, so the gather is spread over 128 threads instead.)
 //
-// Roles per CTA (6 warps): warp 0 gathers (one lane), warp 1 issues the MMAs in
-// CTA 0 and relays CTA 1's "ready" events to CTA 0, warps 2-5 run the online
-// softmax (base 2, lazy rescaling of O when the running max grows by more than
-// 2^8) and the epilogue.  TMEM lane l holds head (l mod 64); lanes l and l+64
+// Roles per CTA (9 warps): warps 0-3 gather, warp 4 issues the MMAs in CTA 0 and
+// relays CTA 1's "ready" events to CTA 0, warps 5-8 run the online softmax (base
+// 2, lazy rescaling of O when the running max grows by more than 2^8) and the
+// epilogue; P is double buffered so softmax(j) overlaps PV(j-1).  TMEM lane l holds head (l mod 64); lanes l and l+64
 // hold the two halves of that head's keys (QK) and output columns (PV), and
 // exchange their block maxima through shared memory.
 #pragma once
@@ -34,7 +36,10 @@
 
 namespace ks {
 
-constexpr int SA_THREADS = 192;
+constexpr int SA_THREADS = 288;
+constexpr int SA_PRODUCERS = 128;  // warps 0-3
+constexpr int SA_MMA_WARP = 4;
+constexpr int SA_SMX_WARP0 = 5;
 constexpr int SA_NB = 64;      // keys per block
 constexpr int SA_HALF = 32;    // keys per CTA in the QK product
 constexpr int SA_MAX_ST = 4;
@@ -42,6 +47,8 @@ constexpr int SA_HDR = 2048;   // shared header bytes
 
 struct SaParams {
   const int32_t* idx;   // [B, M, K]
+  const uint16_t* kv;   // bf16 [B, N, D]
+  int32_t pv_col[2][4]; // first column (relative to dv_begin) of each 64-column V block, per CTA
   const float* sink;    // [H]
   uint16_t* out;        // bf16 [B, M, H, dv]
   int32_t B, M, H, D, N, K;
@@ -50,6 +57,7 @@ struct SaParams {
   int32_t pv_n[2];      // N of each (128 or 256)
   int32_t n_pvblk;      // 64-column V blocks per CTA
   int32_t nst, nblk;
+  int32_t idx_vec4;     // indices may be read as int4 (K % 4 == 0, 16-byte aligned)
   uint32_t q_off, p_off, st_off, st_bytes, sreg_bytes;
   float scale_log2;     // softmax_scale * log2(e)
   int* status;
@@ -59,7 +67,9 @@ struct SaParams {
 struct SaShared {
   uint64_t full[SA_MAX_ST], peer_full[SA_MAX_ST], empty[SA_MAX_ST];
   uint64_t s_full[2];
-  uint64_t p_full, peer_p_full, p_free, o_full, q_full, peer_q, drain;
+  // per P buffer: phase k of p_full[b] / peer_p_full[b] / p_free[b] is block b + 2k,
+  // so none of them can run two phases ahead of its consumer
+  uint64_t p_full[2], peer_p_full[2], p_free[2], o_full, q_full, peer_q, drain;
   uint64_t xchg[3];
   uint64_t mask[SA_MAX_ST];
   uint32_t tmem_base;
@@ -75,8 +85,7 @@ __device__ __forceinline__ float ex2f(float x) {
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
-    sparse_attn_kernel(const __grid_constant__ CUtensorMap qmap,
-                       const __grid_constant__ CUtensorMap kvmap, SaParams p) {
+    sparse_attn_kernel(const __grid_constant__ CUtensorMap qmap, SaParams p) {
   extern __shared__ uint8_t sa_raw[];
   const uint32_t raw = smem_u32(sa_raw);
   uint8_t* smem = sa_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -94,24 +103,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.nst; ++i) {
-      mbar_init(&sh->full[i], 1);
+      mbar_init(&sh->full[i], SA_PRODUCERS);
       mbar_init(&sh->peer_full[i], 1);
       mbar_init(&sh->empty[i], 1);
     }
     mbar_init(&sh->s_full[0], 1);
     mbar_init(&sh->s_full[1], 1);
-    mbar_init(&sh->p_full, 128);
-    mbar_init(&sh->peer_p_full, 1);
-    mbar_init(&sh->p_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh->p_full[i], 128);
+      mbar_init(&sh->peer_p_full[i], 1);
+    }
+    mbar_init(&sh->p_free[0], 1);
+    mbar_init(&sh->p_free[1], 1);
     mbar_init(&sh->o_full, 1);
-    mbar_init(&sh->q_full, 1);
+    mbar_init(&sh->q_full, 1);  // TMA of the query tile
     mbar_init(&sh->peer_q, 1);
     mbar_init(&sh->drain, 1);
     for (int i = 0; i < 3; ++i) mbar_init(&sh->xchg[i], 128);
     sh->abort = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == SA_MMA_WARP) {
     tmem_alloc<2>(&sh->tmem_base, 512);
     tmem_relinquish<2>();
   }
@@ -120,86 +132,78 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ gathers (TMA)
-    if (lane == 0) {
+  if (warp < SA_PRODUCERS / 32) {
+    // ------------------------------------------------------------ gathers (cp.async)
+    // Thread t copies 16-byte chunk (t % 8) of rows r = t/8 + 16 i (i < 4) of every
+    // block: of all 64 keys for this CTA's V columns, and of its own 32 keys for
+    // all D columns.  Indices are loaded one block ahead.
+    const int t = threadIdx.x;
+    const int c = t & 7, rg = t >> 3;
+    if (t == 0) {
       tma_prefetch_desc(&qmap);
-      tma_prefetch_desc(&kvmap);
       mbar_expect_tx(&sh->q_full, (uint32_t)nkb * 8192u);
       const int32_t qrow = (int32_t)(token * p.H + cta * 64);
       for (int d = 0; d < nkb; ++d) tma_load_2d(&qmap, &sh->q_full, qs + d * 8192, d * 64, qrow);
-      const int32_t* ip = p.idx + token * p.K;
-      const uint32_t stage_tx = (uint32_t)(nkb * SA_HALF + p.n_pvblk * SA_NB) * 128u;
-      int issued = 0;
-      for (int j = 0; j < p.nblk; ++j) {
-        const int st = j % p.nst;
-        if (!mbar_wait(&sh->empty[st], ((j / p.nst) & 1) ^ 1, wc)) break;
-        int32_t rows[SA_NB];
-        uint64_t mask = 0;
-#pragma unroll
-        for (int i = 0; i < SA_NB; ++i) {
-          const int kk = j * SA_NB + i;
-          const int32_t v = kk < p.K ? __ldg(ip + kk) : -1;
-          const bool ok = v >= 0 && v < p.N;
-          mask |= (uint64_t)ok << i;
-          rows[i] = b * p.N + (ok ? v : 0);
-        }
-        sh->mask[st] = mask;
-        mbar_expect_tx(&sh->full[st], stage_tx);
-        uint8_t* sreg = stg + st * p.st_bytes;
-        for (int d = 0; d < nkb; ++d) {
-#pragma unroll
-          for (int g = 0; g < SA_HALF / 4; ++g) {
-            const int r = cta * SA_HALF + 4 * g;
-            tma_gather4(&kvmap, &sh->full[st], sreg + d * 4096 + g * 512, d * 64, rows[r],
-                        rows[r + 1], rows[r + 2], rows[r + 3]);
-          }
-        }
-        uint8_t* pvreg = sreg + p.sreg_bytes;
-        int u = 0;
-        for (int i = 0; i < p.n_pv; ++i) {
-          const int hn = p.pv_n[i] / 2;
-          for (int v = 0; v < hn / 64; ++v, ++u) {
-            const int col = p.dv_begin + 256 * i + (int)cta * hn + 64 * v;
-#pragma unroll
-            for (int g = 0; g < SA_NB / 4; ++g)
-              tma_gather4(&kvmap, &sh->full[st], pvreg + u * 8192 + g * 512, col, rows[4 * g],
-                          rows[4 * g + 1], rows[4 * g + 2], rows[4 * g + 3]);
-          }
-        }
-        ++issued;
-      }
-      for (int i = issued > p.nst ? issued - p.nst : 0; i < issued; ++i)
-        mbar_wait(&sh->full[i % p.nst], (i / p.nst) & 1, wc, false, true);
-      mbar_wait(&sh->q_full, 0, wc, false, true);
     }
-  } else if (warp == 1) {
+    const int32_t* ip = p.idx + token * p.K;
+    const uint16_t* kvb = p.kv + (int64_t)b * p.N * p.D;
+    int32_t cur[4], nxt[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = rg + 16 * i;
+      cur[i] = k < p.K ? __ldg(ip + k) : -1;
+    }
+    for (int j = 0; j < p.nblk; ++j) {
+      const int st = j % p.nst;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = (j + 1) * SA_NB + rg + 16 * i;
+        nxt[i] = (j + 1 < p.nblk && k < p.K) ? __ldg(ip + k) : -1;
+      }
+      if (!mbar_wait(&sh->empty[st], ((j / p.nst) & 1) ^ 1, wc)) break;
+      uint8_t* sreg = stg + st * p.st_bytes;
+      uint8_t* pvreg = sreg + p.sreg_bytes;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = rg + 16 * i;
+        const bool ok = cur[i] >= 0 && cur[i] < p.N;
+        const uint16_t* row = kvb + (int64_t)(ok ? cur[i] : 0) * p.D;
+        const uint32_t sw = (uint32_t)((c ^ (r & 7)) << 4);
+        for (int u = 0; u < p.n_pvblk; ++u) {
+          const int col = p.dv_begin + p.pv_col[cta][u] + 8 * c;
+          cp_async16(pvreg + u * 8192 + r * 128 + sw, row + (col < p.D ? col : 0), col < p.D ? 16u : 0u);
+        }
+        if ((r >> 5) == (int)cta) {
+          const int rs = r & 31;
+          for (int d = 0; d < nkb; ++d)
+            cp_async16(sreg + d * 4096 + rs * 128 + sw, row + 64 * d + 8 * c);
+        }
+      }
+      cp_async_arrive(&sh->full[st]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) cur[i] = nxt[i];
+    }
+    cp_async_wait_all();
+    if (t == 0) mbar_wait(&sh->q_full, 0, wc, false, true);
+  } else if (warp == SA_MMA_WARP) {
     if (lane == 0 && cta == 0) {
       // ---------------------------------------------------------- MMA issuer (leader CTA)
+      // Issues S(j) and PV(j) in whichever order their inputs become ready:
+      // S(j) needs both CTAs' gathers of block j and S buffer j%2 free (PV(j-2)
+      // issued); PV(j) needs both CTAs' P(j).
       const uint32_t qaddr = smem_u32(qs), paddr = smem_u32(ps);
       const uint32_t idesc_s = idesc_bf16_f32(128, SA_NB, false, false);
       bool ok = mbar_wait(&sh->q_full, 0, wc) && mbar_wait(&sh->peer_q, 0, wc, true);
-      for (int j = 0; ok && j <= p.nblk; ++j) {
-        if (j < p.nblk) {
-          const int st = j % p.nst;
-          const uint32_t ph = (j / p.nst) & 1;
-          if (!(ok = mbar_wait(&sh->full[st], ph, wc))) break;
-          if (!(ok = mbar_wait(&sh->peer_full[st], ph, wc, true))) break;
+      int ns = 0, npv = 0;
+      uint64_t t0 = clock64();
+      const uint64_t lim = budget_cycles(p.budget_ns);
+      while (ok && npv < p.nblk) {
+        bool progress = false;
+        if (npv < ns && mbar_poll(smem_u32(&sh->p_full[npv & 1]), (npv >> 1) & 1) &&
+            mbar_poll_cluster(smem_u32(&sh->peer_p_full[npv & 1]), (npv >> 1) & 1)) {
           tc_fence_after();
-          const uint32_t sreg = smem_u32(stg + st * p.st_bytes);
-          const uint32_t d_s = tmem + (j & 1) * 32;
-          for (int k = 0; k < p.D / 16; ++k) {
-            const uint64_t ad = sdesc_sw128(qaddr + (k >> 2) * 8192 + (k & 3) * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(sreg + (k >> 2) * 4096 + (k & 3) * 32, 16, 1024);
-            umma_bf16_ss_cg2(d_s, ad, bd, idesc_s, k > 0 ? 1u : 0u);
-          }
-          umma_commit_cg2(&sh->s_full[j & 1], 3);
-        }
-        if (j >= 1) {
-          const int jj = j - 1, st = jj % p.nst;
-          if (!(ok = mbar_wait(&sh->p_full, jj & 1, wc))) break;
-          if (!(ok = mbar_wait(&sh->peer_p_full, jj & 1, wc, true))) break;
-          tc_fence_after();
+          fence_proxy_async_smem();
+          const int st = npv % p.nst;
           const uint32_t pvreg = smem_u32(stg + st * p.st_bytes) + p.sreg_bytes;
           uint32_t ocol = tmem + 64;
           int u = 0;
@@ -207,15 +211,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
             const uint32_t idesc_pv = idesc_bf16_f32(128, p.pv_n[i], false, true);
 #pragma unroll
             for (int kk = 0; kk < SA_NB / 16; ++kk) {
-              const uint64_t ad = sdesc_sw128(paddr + kk * 32, 16, 1024);
+              const uint64_t ad = sdesc_sw128(paddr + (npv & 1) * 8192 + kk * 32, 16, 1024);
               const uint64_t bd = sdesc_sw128(pvreg + u * 8192 + kk * 2048, 8192, 1024);
-              umma_bf16_ss_cg2(ocol, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+              umma_bf16_ss_cg2(ocol, ad, bd, idesc_pv, (npv > 0 || kk > 0) ? 1u : 0u);
             }
             ocol += p.pv_n[i] / 2;
             u += p.pv_n[i] / 128;
           }
           umma_commit_cg2(&sh->empty[st], 3);
-          umma_commit_cg2(&sh->p_free, 3);
+          umma_commit_cg2(&sh->p_free[npv & 1], 3);
+          ++npv;
+          progress = true;
+        }
+        if (ns < p.nblk && ns <= npv + 1) {
+          const int st = ns % p.nst;
+          const uint32_t ph = (ns / p.nst) & 1;
+          if (mbar_poll(smem_u32(&sh->full[st]), ph) &&
+              mbar_poll_cluster(smem_u32(&sh->peer_full[st]), ph)) {
+            tc_fence_after();
+            fence_proxy_async_smem();
+            const uint32_t sreg = smem_u32(stg + st * p.st_bytes);
+            const uint32_t d_s = tmem + (ns & 1) * 32;
+            for (int k = 0; k < p.D / 16; ++k) {
+              const uint64_t ad = sdesc_sw128(qaddr + (k >> 2) * 8192 + (k & 3) * 32, 16, 1024);
+              const uint64_t bd = sdesc_sw128(sreg + (k >> 2) * 4096 + (k & 3) * 32, 16, 1024);
+              umma_bf16_ss_cg2(d_s, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+            }
+            umma_commit_cg2(&sh->s_full[ns & 1], 3);
+            ++ns;
+            progress = true;
+          }
+        }
+        if (progress) {
+          t0 = clock64();
+        } else if (*wc.abort) {
+          ok = false;
+        } else if ((uint64_t)clock64() - t0 > lim) {
+          raise_error(wc, DEV_TIMEOUT);
+          ok = false;
         }
       }
       if (ok) umma_commit_cg2(&sh->o_full, 3);
@@ -223,21 +256,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       mbar_wait(&sh->drain, 0, wc, false, true);
     } else if (lane == 0) {
       // ---------------------------------------------------------- relay (CTA 1)
+      // Forwards "my gathers of block j landed" and "my P(j) is written" to the
+      // leader CTA, each stream in order, whichever is ready first.
       bool ok = mbar_wait(&sh->q_full, 0, wc);
       if (ok) mbar_arrive_cluster(&sh->peer_q, 0);
-      for (int j = 0; ok && j <= p.nblk; ++j) {
-        if (j < p.nblk) {
-          const int st = j % p.nst;
-          if (!(ok = mbar_wait(&sh->full[st], (j / p.nst) & 1, wc))) break;
-          mbar_arrive_cluster(&sh->peer_full[st], 0);
+      int nf = 0, np = 0;
+      uint64_t t0 = clock64();
+      const uint64_t lim = budget_cycles(p.budget_ns);
+      while (ok && np < p.nblk) {
+        bool progress = false;
+        if (nf < p.nblk && mbar_poll(smem_u32(&sh->full[nf % p.nst]), (nf / p.nst) & 1)) {
+          mbar_arrive_cluster(&sh->peer_full[nf % p.nst], 0);
+          ++nf;
+          progress = true;
         }
-        if (j >= 1) {
-          if (!(ok = mbar_wait(&sh->p_full, (j - 1) & 1, wc))) break;
-          mbar_arrive_cluster(&sh->peer_p_full, 0);
+        if (np < nf && mbar_poll(smem_u32(&sh->p_full[np & 1]), (np >> 1) & 1)) {
+          mbar_arrive_cluster(&sh->peer_p_full[np & 1], 0);
+          ++np;
+          progress = true;
+        }
+        if (progress) {
+          t0 = clock64();
+        } else if (*wc.abort) {
+          ok = false;
+        } else if ((uint64_t)clock64() - t0 > lim) {
+          raise_error(wc, DEV_TIMEOUT);
+          ok = false;
         }
       }
     }
-  } else {
+  } else if (warp >= SA_SMX_WARP0) {
     // ------------------------------------------------------------ softmax + epilogue
     const int q4 = warp & 3;
     const int l = q4 * 32 + lane;  // TMEM lane of this thread
@@ -248,18 +296,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
     float m_used = sink2, lsum = 0.f;
     const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
     const int o_cols = p.dv_pad / 2;
+    const int32_t* ip = p.idx + token * p.K + 32 * half;  // this lane's 32 keys of a block
+    // validity bits of this lane's 32 keys of block j (warp-uniform loads)
+    auto valid_bits = [&](int j) -> uint32_t {
+      uint32_t mk = 0;
+      const int k0 = j * SA_NB + 32 * half;
+      if (p.idx_vec4 && k0 + 32 <= p.K) {
+        const int4* v4 = reinterpret_cast<const int4*>(ip + j * SA_NB);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int4 v = __ldg(v4 + q);
+          mk |= (uint32_t)(v.x >= 0 && v.x < p.N) << (4 * q);
+          mk |= (uint32_t)(v.y >= 0 && v.y < p.N) << (4 * q + 1);
+          mk |= (uint32_t)(v.z >= 0 && v.z < p.N) << (4 * q + 2);
+          mk |= (uint32_t)(v.w >= 0 && v.w < p.N) << (4 * q + 3);
+        }
+      } else {
+        for (int i = 0; i < 32; ++i) {
+          const int k = k0 + i;
+          const int32_t v = k < p.K ? __ldg(ip + j * SA_NB + i) : -1;
+          mk |= (uint32_t)(v >= 0 && v < p.N) << i;
+        }
+      }
+      return mk;
+    };
+    uint32_t mk_next = valid_bits(0);
     bool ok = true;
     for (int j = 0; j < p.nblk; ++j) {
-      const int sb = j & 1, st = j % p.nst;
+      const int sb = j & 1;
+      const uint32_t mk = mk_next;
+      if (j + 1 < p.nblk) mk_next = valid_bits(j + 1);
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->s_full[sb], (j >> 1) & 1, wc));
       if (!ok) break;
       tc_fence_after();
       uint32_t r[32];
       tmem_ld32(lane_base + sb * 32, r);
       tmem_wait_ld();
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->full[st], (j / p.nst) & 1, wc));
-      if (!ok) break;
-      const uint32_t mk = (uint32_t)(sh->mask[st] >> (half * 32));
       float s2[32];
       float bmax = -INFINITY;
 #pragma unroll
@@ -287,24 +359,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         lsum += e0 + e1;
         pk[i] = cvt_bf16x2(e0, e1);
       }
-      if (j >= 1) {
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->p_free, (j - 1) & 1, wc));
+      // P buffer j%2 is free once PV(j-2) is done
+      if (j >= 2) {
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->p_free[sb], ((j >> 1) - 1) & 1, wc));
         if (!ok) break;
-        if (__any_sync(0xFFFFFFFFu, resc)) {  // TMEM access is warp-wide; alpha = 1 elsewhere
-          tc_fence_after();
-          for (int c = 0; c < o_cols; c += 16) {
-            uint32_t o[16];
-            tmem_ld16(lane_base + 64 + c, o);
-            tmem_wait_ld();
+      }
+      // rescaling O needs PV(j-1) done (rare: the running max rose by > 2^8)
+      if (j >= 1 && __any_sync(0xFFFFFFFFu, resc)) {  // TMEM access is warp-wide; alpha = 1 elsewhere
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->p_free[sb ^ 1], ((j - 1) >> 1) & 1, wc));
+        if (!ok) break;
+        tc_fence_after();
+        for (int c = 0; c < o_cols; c += 16) {
+          uint32_t o[16];
+          tmem_ld16(lane_base + 64 + c, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
-            tmem_st16(lane_base + 64 + c, o);
-          }
-          tmem_wait_st();
+          for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+          tmem_st16(lane_base + 64 + c, o);
         }
+        tmem_wait_st();
       }
       // P row m, keys [32*half, 32*half + 32) -> 16-byte chunks 4*half .. 4*half+3
-      uint8_t* prow = ps + m * 128;
+      uint8_t* prow = ps + sb * 8192 + m * 128;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         const int c = half * 4 + cc;
@@ -313,7 +389,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&sh->p_full);
+      mbar_arrive(&sh->p_full[sb]);
     }
     if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->o_full, 0, wc));
     if (ok) {
@@ -352,7 +428,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc<2>(tmem, 512);
+  if (warp == SA_MMA_WARP) tmem_dealloc<2>(tmem, 512);
 }
 
 }  // namespace ks
