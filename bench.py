@@ -69,9 +69,11 @@ class DsaE2E(Workload):
     """C5: indexer -> sparse attention, plus Sinkhorn."""
     name = "dsa_e2e"
 
-    def __init__(self, rank, world, device, B=2, S=32768, H_ix=64, D_ix=128, rd=64, k=2048,
-                 H_sa=128, D_sa=576, dv=512, sk_shape=(2, 32768, 8, 8), sk_repeat=20):
+    def __init__(self, rank, world, device, tokens=None, B=2, S=32768, H_ix=64, D_ix=128, rd=64,
+                 k=2048, H_sa=128, D_sa=576, dv=512, sk_shape=(2, 32768, 8, 8), sk_repeat=20):
         super().__init__(rank, world, device)
+        S = tokens or S
+        sk_shape = (sk_shape[0], tokens or sk_shape[1], sk_shape[2], sk_shape[3])
         self.B, self.S, self.H_ix, self.D_ix, self.rd, self.k = B, S, H_ix, D_ix, rd, k
         self.H_sa, self.D_sa, self.dv = H_sa, D_sa, dv
         self.sk_shape, self.sk_repeat = sk_shape, sk_repeat
@@ -106,6 +108,9 @@ class DsaE2E(Workload):
         self.sk_out = torch.empty_like(self.sk_x)
         self.ws = torch.empty(max(ops.indexer_workspace_size(B, b - a, S) for a, b in self.ranges),
                               dtype=torch.uint8, device=dev)
+
+    def work(self):
+        return self.flops(), "tensor"
 
     def flops(self):
         """Algorithmic FLOPs per step on this rank (causal-valid pairs for the indexer)."""
@@ -207,6 +212,221 @@ class DsaE2E(Workload):
                                f"extrapolated to the full step")
 
 
+class SingleOp(Workload):
+    """One operator at one BASELINE.json configuration (C1-C4, or C5's Sinkhorn
+    stage): rows split contiguously over ranks.  `tokens` limits the query rows
+    per batch (small cases for profiling)."""
+
+    def __init__(self, rank, world, device, tokens=None):
+        super().__init__(rank, world, device)
+        self._host = None
+        self.tokens = tokens
+
+    def launches_per_step(self):
+        return self.launches
+
+    def host_buffers(self):
+        import torch
+
+        def pin(t):
+            return torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t)
+
+        if self._host is None:
+            self._host = {"in": [pin(t) for t in self.inputs], "out": [pin(t) for t in self.outputs]}
+        return self._host
+
+    def run_e2e(self):
+        h = self.host_buffers()
+        for d, s in zip(self.inputs, h["in"]):
+            d.copy_(s, non_blocking=True)
+        self.run()
+        for d, s in zip(h["out"], self.outputs):
+            d.copy_(s, non_blocking=True)
+
+    def e2e_bytes(self):
+        nb = lambda ts: sum(t.numel() * t.element_size() for t in ts)
+        return nb(self.inputs), nb(self.outputs)
+
+    def config(self):
+        return {"workload": self.desc, "global_batch": self.B, "seq_len": self.S,
+                "parallelism": f"rows{self.world}", "sharding": "contiguous rows",
+                "l2": self.l2}
+
+
+class SinkhornOp(SingleOp):
+    """C1 (8, 4096, 4, 4) or C5's Sinkhorn stage (2, 32768, 8, 8); repeat = 20."""
+
+    def __init__(self, rank, world, device, tokens=None, shape=(8, 4096, 4, 4)):
+        super().__init__(rank, world, device, tokens)
+        self.B, self.S, self.n = shape[0], (tokens or shape[1]), shape[2]
+        self.units = self.B * self.S
+        self.metric = "matrices/s"
+        self.dtype = "f32"
+        self.desc = f"Sinkhorn fp32 ({self.B}, {self.S}, {self.n}, {self.n}), 20 iterations, eps 1e-6"
+        self.l2 = "L2 flushed between steps (write of a 256 MB buffer)"
+        self.launches = 1
+        if device is None:
+            return
+        import torch
+        from kernelswift_b200 import shard
+
+        m0, m1 = (shard.contiguous(self.units, world, rank) or [(0, 0)])[0]
+        g = torch.Generator(device=device).manual_seed(7 + rank)
+        self.x = torch.randn(m1 - m0, self.n, self.n, device=device, generator=g)
+        self.out = torch.empty_like(self.x)
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+        self.inputs, self.outputs = [self.x], [self.out]
+
+    def work(self):
+        nbytes = 2 * self.x.numel() * 4
+        return {"sinkhorn": nbytes}, "hbm"
+
+    def run(self, timers=None):
+        from kernelswift_b200 import ops
+
+        if timers is not None:
+            self.flush.zero_()  # keep each step's input out of L2
+        with _span(timers, "sinkhorn"):
+            ops.sinkhorn(self.x, 20, 1e-6, out=self.out)
+
+    def cpu_sample(self, budget_rows=None):
+        from oracle import ks_oracle as O
+
+        n = min(self.units, 65536)
+        x = np.random.default_rng(0).standard_normal((n, self.n, self.n)).astype(np.float32)
+        t0 = time.perf_counter()
+        O.sinkhorn(x, 20, 1e-6)
+        dt = time.perf_counter() - t0
+        return n / dt, f"{n} matrices"
+
+
+class SparseAttnOp(SingleOp):
+    """C2 (1, 128, 16, 128; N 4096; K 512) or C4 (4, 4096, 128, 576; N 32768; K 2048; dv 512)."""
+
+    def __init__(self, rank, world, device, tokens=None, cfg="c4"):
+        super().__init__(rank, world, device, tokens)
+        if cfg == "c2":
+            self.B, M, self.H, self.D, self.N, self.K, self.dv = 1, 128, 16, 128, 4096, 512, 128
+        else:
+            self.B, M, self.H, self.D, self.N, self.K, self.dv = 4, 4096, 128, 576, 32768, 2048, 512
+        self.S = tokens or M
+        self.units = self.B * self.S
+        self.desc = (f"SparseAttention bf16 q ({self.B}, {self.S}, {self.H}, {self.D}), kv ({self.B}, "
+                     f"{self.N}, {self.D}) shared latent, top-{self.K} int32 indices "
+                     f"({'randperm' if cfg == 'c2' else 'causal-valid'}), dv {self.dv}")
+        self.l2 = "inputs larger than L2" if cfg == "c4" else "L2 flushed between steps"
+        self.launches = 1
+        self.cfg = cfg
+        if device is None:
+            return
+        import torch
+        from kernelswift_b200 import shard
+
+        m0, m1 = (shard.contiguous(self.S, world, rank) or [(0, 0)])[0]
+        g = torch.Generator(device=device).manual_seed(11 + rank)
+        n = m1 - m0
+        self.q = torch.randn(self.B, n, self.H, self.D, device=device, generator=g).bfloat16()
+        self.kv = torch.randn(self.B, self.N, self.D, device=device, generator=g).bfloat16()
+        if cfg == "c2":
+            self.idx = torch.stack([torch.stack([torch.randperm(self.N, device=device, generator=g)[:self.K]
+                                                 for _ in range(n)]) for _ in range(self.B)]).int()
+        else:  # query m at position N - M + m attends to positions <= its own
+            pos = self.N - M + m0 + torch.arange(n, device=device)
+            r = torch.rand(self.B, n, self.K, device=device, generator=g)
+            self.idx = (r * (pos[None, :, None] + 1).float()).long().clamp_max(self.N - 1).int()
+        self.sink = torch.zeros(self.H, device=device)
+        self.out = torch.empty(self.B, n, self.H, self.dv, dtype=torch.bfloat16, device=device)
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+        self.inputs, self.outputs = [self.q, self.idx], [self.out]
+        self.rows = n
+
+    def work(self):
+        return {"sparse_attn": 2 * self.B * self.rows * self.H * self.K * (self.D + self.dv)}, "tensor"
+
+    def run(self, timers=None):
+        from kernelswift_b200 import ops
+
+        if timers is not None and self.cfg == "c2":
+            self.flush.zero_()
+        with _span(timers, "sparse_attn"):
+            ops.sparse_attn(self.q, self.kv, self.sink, self.idx, self.D ** -0.5, self.dv, out=self.out)
+
+    def cpu_sample(self, budget_rows=(8,)):
+        from oracle import ks_oracle as O
+
+        rng = np.random.default_rng(0)
+        n = budget_rows[0]
+        kv = O.f32_to_bf16(rng.standard_normal((1, self.N, self.D)).astype(np.float32))
+        q = O.f32_to_bf16(rng.standard_normal((1, n, self.H, self.D)).astype(np.float32))
+        idx = np.stack([rng.permutation(self.N)[: self.K] for _ in range(n)])[None].astype(np.int32)
+        t0 = time.perf_counter()
+        O.sparse_attn(q, kv, np.zeros(self.H, np.float32), idx, self.D ** -0.5, self.dv)
+        dt = time.perf_counter() - t0
+        return n / dt, f"{n} query rows, time per row"
+
+
+class IndexerOp(SingleOp):
+    """C3: q (1, 4096, 64, 128) before RoPE, keys (1, 4096, 128), rope 64, top-2048, causal."""
+
+    def __init__(self, rank, world, device, tokens=None):
+        super().__init__(rank, world, device, tokens)
+        self.B, self.H, self.D, self.rd, self.k = 1, 64, 128, 64, 2048
+        self.S = tokens or 4096
+        self.T = self.S
+        self.units = self.B * self.S
+        self.desc = (f"Indexer bf16 q ({self.B}, {self.S}, {self.H}, {self.D}) before RoPE, keys "
+                     f"({self.B}, {self.T}, {self.D}), RoPE on the last {self.rd} dims, causal, "
+                     f"top-{self.k} int64")
+        self.l2 = "inputs larger than L2"
+        if device is None:
+            return
+        import torch
+        from kernelswift_b200 import ops, shard
+
+        self.ranges = shard.zigzag(self.S, world, rank)
+        self.launches = 2 * len(self.ranges)
+        g = torch.Generator(device=device).manual_seed(13 + rank)
+        self.kx = torch.randn(self.B, self.T, self.D, device=device, generator=g).bfloat16()
+        self.q, self.w, self.fr, self.out = [], [], [], []
+        for a, b in self.ranges:
+            self.q.append(torch.randn(self.B, b - a, self.H, self.D, device=device, generator=g).bfloat16())
+            self.w.append((torch.rand(self.B, b - a, self.H, device=device, generator=g) *
+                           (self.D ** -0.5 * self.H ** -0.5)).bfloat16())
+            self.fr.append(_freqs(b - a, self.rd, a).to(device))
+            self.out.append(torch.empty(self.B, b - a, self.k, dtype=torch.int64, device=device))
+        self.ws = torch.empty(max(ops.indexer_workspace_size(self.B, b - a, self.T) for a, b in self.ranges),
+                              dtype=torch.uint8, device=device)
+        self.inputs, self.outputs = self.q + self.w, self.out
+
+    def work(self):
+        return {"indexer": sum(2 * self.H * self.D * self.B * ((a + 1 + b) * (b - a) // 2)
+                               for a, b in self.ranges)}, "tensor"
+
+    def run(self, timers=None):
+        from kernelswift_b200 import ops
+
+        for i, (a, b) in enumerate(self.ranges):
+            with _span(timers, "indexer"):
+                ops.indexer_topk(self.q[i], self.kx, self.w[i], self.fr[i], self.rd, self.T, self.k,
+                                 1, True, 0, pos0=a, out=self.out[i], workspace=self.ws)
+
+    def cpu_sample(self, budget_rows=(8,)):
+        from oracle import ks_oracle as O
+
+        rng = np.random.default_rng(0)
+        n = budget_rows[0]
+        kx = O.f32_to_bf16(rng.standard_normal((1, self.T, self.D)).astype(np.float32))
+        t_ix = 0.0
+        for s in np.linspace(0, self.S - 1, n).astype(int):
+            q = O.f32_to_bf16(rng.standard_normal((1, 1, self.H, self.D)).astype(np.float32))
+            w = O.f32_to_bf16(rng.uniform(0, 0.01, (1, 1, self.H)).astype(np.float32))
+            t0 = time.perf_counter()
+            O.indexer_forward(q, kx[:, : s + 1], w, _freqs(1, self.rd, int(s)).numpy(), self.rd,
+                              self.k, 1, 0, 0, s0=int(s))
+            t_ix += time.perf_counter() - t0
+        return n / t_ix, f"{n} rows spread over positions 0..{self.S - 1}, time per row"
+
+
 def _span(timers, name):
     return timers.span(name) if timers is not None else _null()
 
@@ -293,7 +513,14 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-WORKLOADS = {"dsa_e2e": DsaE2E}
+WORKLOADS = {
+    "dsa_e2e": DsaE2E,
+    "c1": lambda r, w, d, tokens=None: SinkhornOp(r, w, d, tokens, (8, 4096, 4, 4)),
+    "c2": lambda r, w, d, tokens=None: SparseAttnOp(r, w, d, tokens, "c2"),
+    "c3": lambda r, w, d, tokens=None: IndexerOp(r, w, d, tokens),
+    "c4": lambda r, w, d, tokens=None: SparseAttnOp(r, w, d, tokens, "c4"),
+    "c5_sinkhorn": lambda r, w, d, tokens=None: SinkhornOp(r, w, d, tokens, (2, 32768, 8, 8)),
+}
 
 
 def parse():
@@ -305,6 +532,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="query rows per batch (small cases for profiling; not a bench line)")
     return ap.parse_args()
 
 
@@ -323,7 +552,7 @@ def main():
     device = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
-    wl = WORKLOADS[a.workload](rank, world, device)
+    wl = WORKLOADS[a.workload](rank, world, device, tokens=a.tokens) if a.tokens else WORKLOADS[a.workload](rank, world, device)
     from kernelswift_b200 import ops
 
     for _ in range(a.warmup):
@@ -379,13 +608,18 @@ def main():
                "ms_per_step": float(t.item()), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
     peaks = measured_peaks()
-    fl = wl.flops()
-    dom = max(fl, key=fl.get)
-    ach = fl[dom] / (spans[dom] / 1e3) / 1e12
-    peak = peaks["bf16_tflops_sustained"]
-    roofline = {"bound": "tensor", "kernel": dom, "achieved": round(ach, 1), "peak": peak,
-                "unit": "TFLOP/s", "frac": round(ach / peak, 4), "traffic": None,
-                "peak_source": f"{peaks['source']} (sustained bf16)",
+    work, bound = wl.work()
+    dom = max(work, key=lambda k: spans.get(k, 0.0))
+    if bound == "tensor":
+        ach = work[dom] / (spans[dom] / 1e3) / 1e12
+        peak, unit, src = peaks["bf16_tflops_sustained"], "TFLOP/s", "sustained bf16"
+    else:
+        ach = work[dom] / (spans[dom] / 1e3) / 1e9
+        peak, unit, src = peaks["hbm_gbs"], "GB/s", "HBM copy"
+    roofline = {"bound": bound, "kernel": dom, "achieved": round(ach, 1), "peak": peak,
+                "unit": unit, "frac": round(ach / peak, 4), "traffic": None,
+                "algorithmic_per_step": work[dom],
+                "peak_source": f"{peaks['source']} ({src})",
                 "per_kernel_ms": {k: round(v, 4) for k, v in spans.items()}}
     line = {"metric": wl.metric, "value": wl.units / (ms / 1e3), "unit": wl.metric, "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -394,6 +628,7 @@ def main():
             "config": wl.config(), "roofline": roofline, "e2e": e2e,
             "gpu_launches": wl.launches_per_step() * a.steps, "clocks": clk}
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        wl.cpu_sample()  # first call pays the BLAS / allocator warm-up
         v, sample = wl.cpu_sample()
         line["cpu_baseline"] = {"value": v, "unit": wl.metric, "cores": os.cpu_count(),
                                 "kind": "port", "sample": sample}
@@ -405,26 +640,27 @@ def main():
 
 
 def reference_arm(a, rank, world):
+    """The reference algorithm (oracle port) on the host cores, each step a bounded
+    row sample of the workload, throughput extrapolated per row."""
     if rank != 0:
         return
-    wl_cls = WORKLOADS[a.workload]
-    wl = wl_cls(0, world, None)
+    wl = WORKLOADS[a.workload](0, world, None)
     vals = []
     sample = ""
     for i in range(a.warmup + a.steps):
-        v, sample = wl.cpu_sample(budget_rows=(4, 4, 4096))
+        v, sample = wl.cpu_sample()
         if i >= a.warmup:
             vals.append(v)
     v = statistics.median(vals)
     cfg = wl.config()
     cfg["parallelism"] = "host cores"
-    line = {"impl": "reference", "metric": "tokens/s", "value": v, "unit": "tokens/s",
-            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": wl.B * wl.S / v * 1e3,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded)", "config": cfg,
-            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+    line = {"impl": "reference", "metric": wl.metric, "value": v, "unit": wl.metric,
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": wl.units / v * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded)", "config": cfg,
+            "cpu_baseline": {"value": v, "unit": wl.metric, "cores": os.cpu_count(), "kind": "port",
                              "sample": sample},
-            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": v, "unit": wl.metric, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
