@@ -119,6 +119,30 @@ int ks_topk_rows(const void* scores, int64_t score_ld, int64_t B, int64_t S, int
                  void* out, int32_t out_dtype, void* stream);
 
 /*
+ * ks_indexer without a workspace argument, for callers that cannot allocate
+ * device memory: processes whose device memory belongs to another allocator
+ * (a framework's caching allocator or a fixed memory pool that must not be
+ * bypassed), latency-critical paths that must not call cudaMalloc (it can
+ * synchronise the device), and hosts such as FFI bindings or plugins that have
+ * no device allocator to call.  It allocates nothing: the
+ * score rows between the two kernels live in a fixed 32 MiB device array inside
+ * the library, so B * S * round_up(T, 8) * 2 must not exceed 33554432 bytes
+ * (larger calls are rejected with KS_ERR_WORKSPACE; split the rows over several
+ * calls).  Every GPU that loads the library holds the array until the process
+ * exits.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture.  All calls on a device share the one array, so calls that
+ * overlap on the GPU (two streams, or two host threads) race on it: serialise
+ * them.  The array keeps the last call's contents; nothing in it needs clearing.
+ * Arguments and results are those of ks_indexer.  No counterpart in the
+ * reference (its host op allocates its score buffer through torch).
+ */
+int ks_indexer_noalloc(const void* q, const void* k, int64_t k_batch_rows, const void* w,
+                       const float* freqs, int64_t B, int64_t S, int64_t H, int64_t D, int64_t T,
+                       int32_t rope_dim, int64_t pos0, int32_t causal, int32_t ratio,
+                       int32_t topk, int64_t offset, void* out, int32_t out_dtype, void* stream);
+
+/*
  * Synchronise `stream`, then read and clear the current device's status word:
  * KS_OK, or KS_ERR_DEVICE when a kernel reported a timed-out wait or a bounds
  * error since the last call.  No counterpart in the reference.

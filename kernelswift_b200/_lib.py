@@ -41,6 +41,9 @@ SIGNATURES = {
                                          _c_i64, _vp]),
     "ks_topk_rows": (ctypes.c_int, [_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i32,
                                     _c_i32, _c_i64, _vp, _c_i32, _vp]),
+    "ks_indexer_noalloc": (ctypes.c_int, [_vp, _vp, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64,
+                                          _c_i64, _c_i64, _c_i32, _c_i64, _c_i32, _c_i32, _c_i32,
+                                          _c_i64, _vp, _c_i32, _vp]),
     "ks_device_status": (ctypes.c_int, [_vp]),
     "ks_selftest_wait_timeout": (ctypes.c_int, [_c_u64, _vp]),
 }

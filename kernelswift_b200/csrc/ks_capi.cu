@@ -332,6 +332,36 @@ __global__ void selftest_wait_kernel(int* status, uint64_t budget_ns) {
   }
 }
 
+// ------------------------------------------------------------------ allocation-free indexer
+// Scratch for ks_indexer_noalloc: the bf16 score rows between the score and top-k
+// kernels live in this fixed array instead of caller-provided memory.  Every GPU
+// that loads the library holds it until the process exits.  In host code the name
+// is only a stand-in for the device array; its device address comes from
+// cudaGetSymbolAddress, once per device.
+constexpr size_t kNoallocScratchBytes = 32u << 20;  // 32 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices];
+
+// Device address of g_noalloc_scratch on the current device (set up on the first
+// call on that device).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(KS_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(indexer scratch)");
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return KS_OK;
+}
+
 }  // namespace
 }  // namespace ks
 
@@ -449,6 +479,33 @@ int ks_device_status(void* stream) {
                 v == DEV_TIMEOUT ? "a bounded wait timed out" : "bounds check failed");
   }
   return KS_OK;
+}
+
+int ks_indexer_noalloc(const void* q, const void* k, int64_t k_batch_rows, const void* w,
+                       const float* freqs, int64_t B, int64_t S, int64_t H, int64_t D, int64_t T,
+                       int32_t rope_dim, int64_t pos0, int32_t causal, int32_t ratio,
+                       int32_t topk, int64_t offset, void* out, int32_t out_dtype,
+                       void* stream) {
+  if (int rc = indexer_check(q, k, w, freqs, B, S, H, D, T, rope_dim, ratio, k_batch_rows)) return rc;
+  if (topk < 1 || topk > 4096) return fail(KS_ERR_UNSUPPORTED, "indexer: topk=%d (1..4096)", topk);
+  if (!out) return fail(KS_ERR_INVALID, "indexer: out is null");
+  if (T == 0) return KS_OK;
+  const size_t need = ks_indexer_workspace_size(B, S, T);
+  if (need > kNoallocScratchBytes)
+    return fail(KS_ERR_WORKSPACE,
+                "indexer_noalloc: B*S*round_up(T,8)*2 = %zu bytes of scores exceeds the fixed "
+                "%zu-byte scratch; split the rows into smaller calls or use ks_indexer",
+                need, kNoallocScratchBytes);
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  // Nothing in the scratch has to start at zero: the score kernel writes every
+  // element the top-k kernel reads (each row's causal prefix).
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t ld = round_up(T, 8);
+  if (int rc = indexer_scores_impl(q, k, k_batch_rows, w, freqs, B, S, H, D, T, rope_dim, pos0,
+                                   causal, ratio, scratch, ld, st))
+    return rc;
+  return topk_impl(scratch, ld, B, S, T, pos0, causal, ratio, topk, offset, out, out_dtype, st);
 }
 
 int ks_selftest_wait_timeout(uint64_t budget_ns, void* stream) {
