@@ -291,22 +291,16 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
   const uint32_t nkb = (uint32_t)(D / 64);
   p.q_off = SA_HDR;
   p.p_off = p.q_off + nkb * 8192;
-  p.s_off = p.p_off + SA_PBYTES;
-  p.v_bytes = (uint32_t)p.n_pvblk * 8192;
-  // ring sizes: as many slots as fit in the 227 KB per-CTA limit (at least 2 each)
+  p.r_off = p.p_off + SA_PBYTES;
+  // ring: as many 16 KB slots as fit in the 227 KB per-CTA limit
   const size_t limit = 232448 - 1024 /* alignment slack */;
-  const size_t avail = limit > p.s_off ? limit - p.s_off : 0;
-  int nv = 2;
-  int ns = (int)((avail - (size_t)nv * p.v_bytes) / SA_SCHUNK);
-  if (ns > SA_MAX_S) ns = SA_MAX_S;
-  if (ns < 2 || avail < (size_t)nv * p.v_bytes)
-    return fail(KS_ERR_UNSUPPORTED, "sparse_attn: shared memory too small for D=%lld dv=%lld", (long long)D, (long long)dv);
-  nv = (int)((avail - (size_t)ns * SA_SCHUNK) / p.v_bytes);
-  if (nv > SA_MAX_V) nv = SA_MAX_V;
-  p.ns_slots = ns;
-  p.nv_slots = nv;
-  p.v_off = p.s_off + (uint32_t)ns * SA_SCHUNK;
-  const size_t smem = 1024 + p.v_off + (size_t)nv * p.v_bytes;
+  const size_t avail = limit > p.r_off ? limit - p.r_off : 0;
+  int ns = (int)(avail / SA_SLOT);
+  if (ns > SA_MAX_SLOTS) ns = SA_MAX_SLOTS;
+  if (ns < SA_GROUPS)
+    return fail(KS_ERR_UNSUPPORTED, "sparse_attn: shared memory too small for D=%lld", (long long)D);
+  p.n_slots = ns;
+  const size_t smem = 1024 + p.r_off + (size_t)ns * SA_SLOT;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = dev->status;
   p.budget_ns = wait_budget_ns();

@@ -87,6 +87,30 @@ __device__ __forceinline__ bool mbar_test_cluster(uint32_t bar, uint32_t parity)
   return ok != 0;
 }
 
+// try_wait that may suspend the thread for up to `hint_ns` (or until the phase
+// completes): a waiting warp sleeps instead of spinning, so it takes no issue
+// slots from the warps that share its scheduler.
+__device__ __forceinline__ bool mbar_test_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_test_sleep_cluster(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;"
+      " selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+constexpr uint32_t kSleepHintNs = 20000;
+
 // Non-blocking probes (mbarrier.test_wait): for loops that poll several barriers;
 // try_wait may suspend the thread on the first incomplete barrier it probes.
 __device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity) {
@@ -133,22 +157,34 @@ __device__ __forceinline__ void raise_error(const WaitCtx& w, int code) {
 // recorded).  `drain` waits are the ones that make sure copies and MMAs already
 // in flight have landed before the CTA exits; they ignore the abort flag but
 // keep the time budget.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitCtx& w,
-                                       bool cluster_scope = false, bool drain = false) {
+__device__ __forceinline__ bool mbar_wait_body(uint64_t* bar, uint32_t parity, const WaitCtx& w,
+                                               bool cluster_scope, bool drain) {
   const uint32_t b = smem_u32(bar);
   if (cluster_scope ? mbar_test_cluster(b, parity) : mbar_test(b, parity)) return true;
   const uint64_t t0 = clock64();
   const uint64_t lim = budget_cycles(w.budget_ns);
-  for (uint32_t it = 1;; ++it) {
-    if (cluster_scope ? mbar_test_cluster(b, parity) : mbar_test(b, parity)) return true;
-    if ((it & 15) == 0) {
-      if (!drain && *w.abort) return false;
-      if ((uint64_t)clock64() - t0 > lim) {
-        raise_error(w, DEV_TIMEOUT);
-        return false;
-      }
+  for (;;) {
+    if (cluster_scope ? mbar_test_sleep_cluster(b, parity, kSleepHintNs)
+                      : mbar_test_sleep(b, parity, kSleepHintNs))
+      return true;
+    if (!drain && *w.abort) return false;
+    if ((uint64_t)clock64() - t0 > lim) {
+      raise_error(w, DEV_TIMEOUT);
+      return false;
     }
   }
+}
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitCtx& w,
+                                       bool cluster_scope = false, bool drain = false) {
+  return mbar_wait_body(bar, parity, w, cluster_scope, drain);
+}
+// The same wait compiled into the caller.  A call keeps every register that is
+// live across it (e.g. the destination of a load still in flight) in a saved
+// register or on the stack, and saving one waits for its load to land: loops
+// that keep loads in flight across a wait use this form.
+__device__ __forceinline__ bool mbar_wait_inl(uint64_t* bar, uint32_t parity, const WaitCtx& w,
+                                              bool cluster_scope = false) {
+  return mbar_wait_body(bar, parity, w, cluster_scope, false);
 }
 
 // ------------------------------------------------------------------ clusters
@@ -197,6 +233,33 @@ __device__ __forceinline__ void tma_gather4(const CUtensorMap* m, uint64_t* bar,
       "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2),
       "r"(y3)
       : "memory");
+}
+
+// ------------------------------------------------------------------ predicated loads
+// 16 bytes from global memory (cached in L2 only) when `pred`, else zeros.  The
+// zeros are written first and the load is predicated, so nothing consumes the
+// loaded value here: the thread runs on until it uses the registers (a
+// `pred ? load : 0` select would wait for the load on the spot).
+__device__ __forceinline__ uint4 ldcg_or_zero(const void* ptr, bool pred) {
+  uint4 v;
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %5, 0;"
+      " mov.b32 %0, 0; mov.b32 %1, 0; mov.b32 %2, 0; mov.b32 %3, 0;"
+      " @p ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4]; }"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(ptr), "r"((int)pred));
+  return v;
+}
+
+// 32-bit load through the read-only path when `pred`, else `fallback` (same idea).
+__device__ __forceinline__ int32_t ldg_s32_or(const int32_t* ptr, bool pred, int32_t fallback) {
+  int32_t v;
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %3, 0; mov.b32 %0, %2;"
+      " @p ld.global.nc.b32 %0, [%1]; }"
+      : "=r"(v)
+      : "l"(ptr), "r"(fallback), "r"((int)pred));
+  return v;
 }
 
 // ------------------------------------------------------------------ cp.async (16 bytes)

@@ -15,43 +15,66 @@
 // one token with cta_group::2 MMAs (M = 128 = 64 heads per CTA): each SM holds
 // the accumulators of its 64 heads.  Keys are processed in blocks of 256:
 //   QK:  S[64 heads, 256 keys] per CTA with N = 256 per instruction; each CTA
-//        supplies 128 of the block's keys as its half of the B operand, streamed
-//        through a ring of 64-dim chunks (128 keys x 64 dims = 16 KB).
-//   PV:  O[64 heads, dv] per CTA += P[64, 256] . V[256, dv] in four 64-key chunks;
-//        each CTA supplies its half of every PV instruction's N columns for the
-//        64 keys of a chunk, streamed through a ring of V chunks.
-// Rows are gathered by 256 threads with 16-byte loads into registers and 16-byte
-// shared stores (the swizzle computed per store) into the 128-byte-swizzled
-// layout the MMAs read (K-major for QK, MN-major for PV).  Random 128-byte rows
-// need many loads in flight: measured per SM, cp.async from 128 threads stays near
-// 50 GB/s whatever the ring depth, register-staged loads from 256 threads reach
-// ~113 GB/s (8 loads in flight each).  Per 256 keys an SM runs 36 + 32 MMAs of 64
-// tensor cycles each and gathers ~275 KB.
+//        supplies 128 of the block's keys as its half of the B operand, in
+//        64-dim chunks (128 keys x 64 dims = 16 KB).
+//   PV:  O[64 heads, dv] per CTA += P[64, 256] . V[256, dv] in eight 32-key
+//        chunks; each CTA supplies its half of every PV instruction's N columns
+//        for the 32 keys of a chunk (up to 16 KB).
+// All chunks go through ONE ring of 16 KB slots in the order the MMAs consume
+// them: S(0) | S(1) V(0) | S(2) V(1) | ... | V(nblk-1), where S(j) = the nkb QK
+// chunks of block j and V(j) its 8 V chunks.  S(j+1) runs on the tensor cores
+// while the softmax of block j works; V(j) follows once P(j) is written.
 //
-// Roles per CTA (13 warps): warps 0-7 gather, warp 8 issues the MMAs in CTA 0 and
-// relays CTA 1's "ready" events to CTA 0 (both with suspending waits, in the
-// order the gathers are produced), warps 9-12 run the online softmax (base
-// 2, lazy rescaling of O when the running max grows by more than 2^8) and the
-// epilogue.  TMEM lane l holds head (l mod 64); lanes l and l+64 hold the two
-// halves of that head's keys (QK) and output columns (PV) and exchange their
-// block maxima through shared memory.
+// Gathers.  Rows are random 128-byte pieces; they are moved with 16-byte loads
+// into registers and 16-byte shared stores (the swizzle computed per store) into
+// the 128-byte-swizzled layouts the MMAs read (K-major for QK, MN-major for PV).
+// A thread's proxy fence and barrier arrive wait for every load it still has in
+// flight, so one thread cannot overlap two chunks; instead four groups of two
+// warps take turns (group g fills chunks g, g + 4, ...): each group loads a whole
+// chunk into registers (16 loads per thread) before its slot is free, so up to
+// 64 KB per SM are in flight while the slots turn over.  Measured per SM on
+// random rows: register-staged loads reach ~120 GB/s with 32 KB in flight;
+// cp.async saturates near 16 KB in flight (~55 GB/s) and TMA tile::gather4 near
+// 48 GB/s with 16 issuing warps.  Per 256 keys an SM runs 36 + 32 MMAs of 64
+// tensor cycles each and gathers ~272 KB.
+//
+// Roles per CTA (16 warps; registers are granted per four warps, so 13 would
+// cost the same):
+//   warps 0-7   four gather groups,
+//   warps 8, 9  issue the MMAs in CTA 0: warp 8 the QK chunks, warp 9 the V
+//               chunks; in CTA 1 warp 8 forwards "query tile landed",
+//   warps 10-11 idle,
+//   warps 12-15 online softmax (base 2, lazy rescaling of O when the running max
+//               grows by more than 2^8) and the epilogue.
+// TMEM lane l holds head (l mod 64); lanes l and l+64 hold the two halves of that
+// head's keys (QK) and output columns (PV) and exchange their block maxima
+// through shared memory.
 #pragma once
 #include "ks_device.cuh"
 
 namespace ks {
 
-constexpr int SA_THREADS = 416;
-constexpr int SA_PRODUCERS = 256;   // warps 0-7
+// Event timestamps of the first CTA pair for pipeline studies: a build that
+// defines KS_SA_TRACE(ev, i) records them; normal builds compile them out.
+#ifndef KS_SA_TRACE
+#define KS_SA_TRACE(ev, i) do { } while (0)
+#endif
+
+constexpr int SA_THREADS = 512;
+constexpr int SA_GROUPS = 4;        // gather groups
+constexpr int SA_GROUP = 64;        // threads per gather group
+constexpr int SA_PROD_WARPS = SA_GROUPS * SA_GROUP / 32;
 constexpr int SA_MMA_WARP = 8;
-constexpr int SA_SMX_WARP0 = 9;
+constexpr int SA_SMX_WARP0 = 12;
+constexpr int SA_SMX_WARPS = 4;
 constexpr int SA_NB = 256;          // keys per block
 constexpr int SA_HALF = 128;        // keys per CTA in the QK product
-constexpr int SA_KC = 64;           // keys per PV chunk
+constexpr int SA_KC = 32;           // keys per V chunk
 constexpr int SA_NKC = SA_NB / SA_KC;
-constexpr int SA_MAX_S = 4;         // QK chunk ring slots
-constexpr int SA_MAX_V = 4;         // V chunk ring slots
+constexpr int SA_MAX_SLOTS = 12;    // ring slots
 constexpr int SA_HDR = 2048;        // shared header bytes
-constexpr uint32_t SA_SCHUNK = SA_HALF * 128;  // 128 keys x 64 dims bf16
+constexpr uint32_t SA_SLOT = SA_HALF * 128;    // 16 KB: 128 keys x 64 dims bf16
+constexpr uint32_t SA_VSEG = SA_KC * 128;      // one 64-column V segment of a chunk
 constexpr uint32_t SA_PBYTES = 64 * SA_NB * 2; // P: 64 heads x 256 keys bf16
 constexpr int SA_SCOLS = SA_NB / 2;            // TMEM columns of one S buffer (2x2 layout)
 constexpr int SA_OCOL = 2 * SA_SCOLS;          // first TMEM column of O
@@ -61,25 +84,24 @@ struct SaParams {
   const uint16_t* kv;   // bf16 [B, N, D]
   const float* sink;    // [H]
   uint16_t* out;        // bf16 [B, M, H, dv]
-  int32_t pv_col[2][4]; // first column (relative to dv_begin) of each 64-column V block, per CTA
+  int32_t pv_col[2][4]; // first column (relative to dv_begin) of each 64-column V segment, per CTA
   int32_t B, M, H, D, N, K;
   int32_t dv_begin, dv, dv_pad;
-  int32_t n_pv;         // PV instructions per 64-key chunk
+  int32_t n_pv;         // PV instructions per 16-key step
   int32_t pv_n[2];      // N of each (128 or 256)
-  int32_t n_pvblk;      // 64-column V blocks per CTA
-  int32_t ns_slots, nv_slots, nblk;
+  int32_t n_pvblk;      // 64-column V segments per CTA
+  int32_t n_slots, nblk;
   int32_t idx_vec4;     // indices may be read as int4 (K % 4 == 0, 16-byte aligned)
-  uint32_t q_off, p_off, s_off, v_off, v_bytes;
+  uint32_t q_off, p_off, r_off;  // query tile, P, ring
   float scale_log2;     // softmax_scale * log2(e)
   int* status;
   uint64_t budget_ns;
 };
 
 struct SaShared {
-  uint64_t s_full[SA_MAX_S], peer_s_full[SA_MAX_S], s_empty[SA_MAX_S];
-  uint64_t v_full[SA_MAX_V], peer_v_full[SA_MAX_V], v_empty[SA_MAX_V];
-  uint64_t acc_full[2];
-  uint64_t p_full, peer_p_full, p_free, o_full, q_full, peer_q, drain;
+  uint64_t full_s[SA_MAX_SLOTS], full_v[SA_MAX_SLOTS], empty[SA_MAX_SLOTS];
+  uint64_t acc_full[2], s_free[2];
+  uint64_t p_full, p_free, o_full, q_full, peer_q, drain_s, drain_v;
   uint64_t xchg[3];
   uint32_t tmem_base;
   int abort;
@@ -91,6 +113,19 @@ __device__ __forceinline__ float ex2f(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// One warp's "my part of this chunk is in shared memory" for the leader CTA's
+// barrier: every lane fences its own stores for the tensor core (async proxy),
+// then one lane arrives, locally in CTA 0 or remotely (release, cluster scope)
+// from CTA 1.
+__device__ __forceinline__ void sa_warp_ready(uint64_t* bar, uint32_t cta, int lane) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (cta == 0) mbar_arrive(bar);
+    else mbar_arrive_cluster(bar, 0);
+  }
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
@@ -110,25 +145,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
   WaitCtx wc{&sh->abort, p.status, p.budget_ns};
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < p.ns_slots; ++i) {
-      mbar_init(&sh->s_full[i], SA_PRODUCERS);
-      mbar_init(&sh->peer_s_full[i], 1);
-      mbar_init(&sh->s_empty[i], 1);
-    }
-    for (int i = 0; i < p.nv_slots; ++i) {
-      mbar_init(&sh->v_full[i], SA_PRODUCERS);
-      mbar_init(&sh->peer_v_full[i], 1);
-      mbar_init(&sh->v_empty[i], 1);
+    for (int i = 0; i < p.n_slots; ++i) {
+      mbar_init(&sh->full_s[i], 2 * (SA_GROUP / 32));  // the filling group's warps, both CTAs
+      mbar_init(&sh->full_v[i], 2 * (SA_GROUP / 32));
+      mbar_init(&sh->empty[i], 1);
     }
     mbar_init(&sh->acc_full[0], 1);
     mbar_init(&sh->acc_full[1], 1);
-    mbar_init(&sh->p_full, 128);
-    mbar_init(&sh->peer_p_full, 1);
+    mbar_init(&sh->s_free[0], 2 * SA_SMX_WARPS);
+    mbar_init(&sh->s_free[1], 2 * SA_SMX_WARPS);
+    mbar_init(&sh->p_full, 2 * SA_SMX_WARPS);
     mbar_init(&sh->p_free, 1);
     mbar_init(&sh->o_full, 1);
     mbar_init(&sh->q_full, 1);  // TMA of the query tile
     mbar_init(&sh->peer_q, 1);
-    mbar_init(&sh->drain, 1);
+    mbar_init(&sh->drain_s, 1);
+    mbar_init(&sh->drain_v, 1);
     for (int i = 0; i < 3; ++i) mbar_init(&sh->xchg[i], 128);
     sh->abort = 0;
     fence_barrier_init();
@@ -141,206 +173,223 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
+  const int32_t* ip = p.idx + token * p.K;
+  const uint16_t* kvb = p.kv + (int64_t)b * p.N * p.D;
+  // Indices are fetched raw (-1 past K) well before they are used and checked
+  // only then, so no thread waits on an index load; a masked key (negative or
+  // beyond N) is gathered as zeros.  Likewise the row loads are predicated loads
+  // that nothing reads until the shared-memory store.
+  auto idx_raw = [&](int key) -> int32_t { return ldg_s32_or(ip + key, key < p.K, -1); };
+  auto idx_ok = [&](int32_t v) -> bool { return v >= 0 && v < p.N; };
 
-  if (warp < SA_PRODUCERS / 32) {
+  // Ring position n -> chunk: S(0) first, then per period p = 1..nblk the
+  // chunks S(p) (p < nblk) followed by V(p - 1).  is_v: V chunk; blk: its block;
+  // sub: dims chunk (QK) or 32-key chunk (V).
+  const uint32_t period = (uint32_t)(nkb + SA_NKC);
+  const uint32_t n_total = (uint32_t)p.nblk * period;
+  auto decode = [&](uint32_t n, bool& is_v, int& blk, int& sub) {
+    if (n < (uint32_t)nkb) {
+      is_v = false; blk = 0; sub = (int)n;
+      return;
+    }
+    const uint32_t m = n - nkb;
+    const int pp = 1 + (int)(m / period), r = (int)(m % period);
+    if (pp < p.nblk && r < nkb) {
+      is_v = false; blk = pp; sub = r;
+    } else {
+      is_v = true; blk = pp - 1; sub = pp < p.nblk ? r - nkb : r;
+    }
+  };
+
+  if (warp < SA_PROD_WARPS) {
     // ------------------------------------------------------------ gathers
-    // Thread t moves 16-byte piece (t % 8) of rows t/8 + 32 i.  Order: the QK
-    // chunks of block j (this CTA's 128 keys, 64 dims each; two chunks per round so
-    // eight loads are in flight), then the V chunks of block j-1 (64 keys, this
-    // CTA's V columns) - the order the MMAs consume them.  Shared stores are
-    // generic-proxy writes: each thread fences them for the tensor core before it
-    // arrives on the slot's barrier.
-    const int t = threadIdx.x;
-    const int c = t & 7, rg = t >> 3;
-    if (t == 0) {
+    // Group g (warps 2g, 2g + 1) fills ring positions g, g + 4, ...  Thread u of
+    // the group moves 16-byte piece c = u % 8 of keys rg + 8 i, rg = u / 8:
+    //   QK chunk: i < 16 (the CTA's 128 keys of the block), dims 64 sub + 8 c;
+    //   V chunk:  i < 4 (keys 32 sub + ..), each of the CTA's n_pvblk V segments.
+    // Row r = rg + 8 i lands at r * 128 + 16 (c ^ rg) of its 1024-byte swizzle
+    // atom.  The raw indices of the group's next chunk are fetched with the
+    // current chunk's loads; the round's fence has waited for them by the time
+    // they are used.
+    const int g = warp >> 1;
+    const int u = ((warp & 1) << 5) | lane;
+    const int c = u & 7, rg = u >> 3;
+    const uint32_t swz = (uint32_t)((c ^ rg) << 4);
+    if (threadIdx.x == 0) {
       tma_prefetch_desc(&qmap);
       mbar_expect_tx(&sh->q_full, (uint32_t)nkb * 8192u);
       const int32_t qrow = (int32_t)(token * p.H + cta * 64);
       for (int d = 0; d < nkb; ++d) tma_load_2d(&qmap, &sh->q_full, qs + d * 8192, d * 64, qrow);
     }
-    const int32_t* ip = p.idx + token * p.K;
-    const uint16_t* kvb = p.kv + (int64_t)b * p.N * p.D;
-    auto idx_at = [&](int key) -> int32_t { return key < p.K ? __ldg(ip + key) : -1; };
-    auto row_of = [&](int32_t v) -> const uint16_t* {
-      return kvb + (int64_t)((v >= 0 && v < p.N) ? v : 0) * p.D;
-    };
-    // indices of this thread's rows, loaded one block ahead:
-    //   s_idx: QK rows of block j (this CTA's keys), v_idx: V rows of block j-1
-    int32_t s_idx[4], v_idx[8];
+    int colv[4];
+    bool colin[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) s_idx[i] = idx_at((int)cta * SA_HALF + rg + 32 * i);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v_idx[i] = -1;
-    uint32_t sc = 0, vc = 0;
-    bool ok = true;
-    for (int j = 0; ok && j <= p.nblk; ++j) {
-      int32_t s_nxt[4], v_nxt[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        s_nxt[i] = j + 1 < p.nblk ? idx_at((j + 1) * SA_NB + (int)cta * SA_HALF + rg + 32 * i) : -1;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)  // chunk i/2, row rg + 32 (i%2)
-        v_nxt[i] = j < p.nblk ? idx_at(j * SA_NB + (i >> 1) * SA_KC + rg + 32 * (i & 1)) : -1;
-      if (j < p.nblk) {
-        const uint16_t* rows[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) rows[i] = row_of(s_idx[i]) + 8 * c;
-        for (int d = 0; d < nkb; d += 2) {
-          const bool two = d + 1 < nkb;
-          uint4 v[8];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            v[i] = __ldcg(reinterpret_cast<const uint4*>(rows[i] + 64 * d));
-            if (two) v[4 + i] = __ldcg(reinterpret_cast<const uint4*>(rows[i] + 64 * (d + 1)));
-          }
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (h == 1 && !two) break;
-            const int slot = sc % p.ns_slots;
-            if (!(ok = mbar_wait(&sh->s_empty[slot], ((sc / p.ns_slots) & 1) ^ 1, wc))) break;
-            uint8_t* dst = smem + p.s_off + slot * SA_SCHUNK;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int r = rg + 32 * i;
-              *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = v[4 * h + i];
-            }
-            fence_proxy_async_smem();
-            mbar_arrive(&sh->s_full[slot]);
-            ++sc;
-          }
-          if (!ok) break;
-        }
-      }
-      if (ok && j >= 1) {
-        for (int kc = 0; kc < SA_NKC; ++kc, ++vc) {
-          uint4 v[8];
-          const uint16_t* row0 = row_of(v_idx[2 * kc]);
-          const uint16_t* row1 = row_of(v_idx[2 * kc + 1]);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (u < p.n_pvblk) {
-              const int col = p.dv_begin + p.pv_col[cta][u] + 8 * c;
-              const bool in = col < p.D;
-              v[2 * u] = in ? __ldcg(reinterpret_cast<const uint4*>(row0 + col)) : make_uint4(0, 0, 0, 0);
-              v[2 * u + 1] = in ? __ldcg(reinterpret_cast<const uint4*>(row1 + col)) : make_uint4(0, 0, 0, 0);
-            }
-          }
-          const int slot = vc % p.nv_slots;
-          if (!(ok = mbar_wait(&sh->v_empty[slot], ((vc / p.nv_slots) & 1) ^ 1, wc))) break;
-          uint8_t* dst = smem + p.v_off + slot * p.v_bytes;
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (u < p.n_pvblk) {
-#pragma unroll
-              for (int i = 0; i < 2; ++i) {
-                const int r = rg + 32 * i;
-                *reinterpret_cast<uint4*>(dst + u * 8192 + r * 128 + ((c ^ (r & 7)) << 4)) = v[2 * u + i];
-              }
-            }
-          }
-          fence_proxy_async_smem();
-          mbar_arrive(&sh->v_full[slot]);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) s_idx[i] = s_nxt[i];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v_idx[i] = v_nxt[i];
+    for (int s = 0; s < 4; ++s) {
+      colv[s] = s < p.n_pvblk ? p.dv_begin + p.pv_col[cta][s] + 8 * c : 0;
+      colin[s] = s < p.n_pvblk && colv[s] < p.D;
     }
-    if (t == 0) mbar_wait(&sh->q_full, 0, wc, false, true);
-  } else if (warp == SA_MMA_WARP) {
-    if (lane == 0 && cta == 0) {
-      // ---------------------------------------------------------- MMA issuer (leader CTA)
-      // Consumption order = production order: the QK chunks of block j, then
-      // P(j-1) and the V chunks of block j-1.  Blocking (suspending) waits.
-      const uint32_t qaddr = smem_u32(qs), paddr = smem_u32(ps);
-      const uint32_t idesc_s = idesc_bf16_f32(128, SA_NB, false, false);
-      bool ok = mbar_wait(&sh->q_full, 0, wc) && mbar_wait(&sh->peer_q, 0, wc, true);
-      uint32_t sc = 0, vc = 0;
-      for (int j = 0; ok && j <= p.nblk; ++j) {
-        if (j < p.nblk) {
-          // S buffer j%2 was last read by softmax(j-2), whose P was consumed by PV(j-2)
-          const uint32_t d_s = tmem + (j & 1) * SA_SCOLS;
-          for (int d = 0; d < nkb; ++d, ++sc) {
-            const int slot = sc % p.ns_slots;
-            const uint32_t ph = (sc / p.ns_slots) & 1;
-            if (!(ok = mbar_wait(&sh->s_full[slot], ph, wc) &&
-                       mbar_wait(&sh->peer_s_full[slot], ph, wc, true)))
-              break;
-            tc_fence_after();
-            fence_proxy_async_smem();
-            const uint32_t saddr = smem_u32(smem + p.s_off + slot * SA_SCHUNK);
+    int32_t nidx[16];
+    auto fetch = [&](uint32_t n) {
+      if (n >= n_total) return;
+      bool is_v;
+      int blk, sub;
+      decode(n, is_v, blk, sub);
+      if (!is_v) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = sdesc_sw128(qaddr + d * 8192 + kk * 32, 16, 1024);
-              const uint64_t bd = sdesc_sw128(saddr + kk * 32, 16, 1024);
-              umma_bf16_ss_cg2(d_s, ad, bd, idesc_s, (d > 0 || kk > 0) ? 1u : 0u);
+        for (int i = 0; i < 16; ++i) nidx[i] = idx_raw(blk * SA_NB + (int)cta * SA_HALF + rg + 8 * i);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) nidx[i] = idx_raw(blk * SA_NB + sub * SA_KC + rg + 8 * i);
+      }
+    };
+    fetch((uint32_t)g);
+    bool ok = true;
+    for (uint32_t n = (uint32_t)g; ok && n < n_total; n += SA_GROUPS) {
+      bool is_v;
+      int blk, sub;
+      decode(n, is_v, blk, sub);
+      uint4 v[16];
+      if (!is_v) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          v[i] = ldcg_or_zero(kvb + (int64_t)nidx[i] * p.D + 64 * sub + 8 * c, idx_ok(nidx[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const bool rok = idx_ok(nidx[i]);
+          const uint16_t* row = kvb + (int64_t)nidx[i] * p.D;
+#pragma unroll
+          for (int s = 0; s < 4; ++s) v[4 * i + s] = ldcg_or_zero(row + colv[s], colin[s] && rok);
+        }
+      }
+      fetch(n + SA_GROUPS);
+      const int slot = (int)(n % (uint32_t)p.n_slots);
+      if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->empty[slot], ((n / p.n_slots) & 1) ^ 1, wc))))
+        break;
+      if (u == 0) KS_SA_TRACE(g, n / SA_GROUPS);
+      uint8_t* dst = smem + p.r_off + slot * SA_SLOT;
+      if (!is_v) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          *reinterpret_cast<uint4*>(dst + (rg + 8 * i) * 128 + swz) = v[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int s = 0; s < 4; ++s)
+            if (s < p.n_pvblk)
+              *reinterpret_cast<uint4*>(dst + s * SA_VSEG + (rg + 8 * i) * 128 + swz) = v[4 * i + s];
+      }
+      sa_warp_ready(is_v ? &sh->full_v[slot] : &sh->full_s[slot], cta, lane);
+      if (u == 0) KS_SA_TRACE(4 + g, n / SA_GROUPS);
+    }
+    if (threadIdx.x == 0) mbar_wait(&sh->q_full, 0, wc, false, true);
+  } else if (warp == SA_MMA_WARP || warp == SA_MMA_WARP + 1) {
+    if (lane == 0 && cta == 0) {
+      // ---------------------------------------------------------- MMA issuers (leader CTA)
+      // Two threads in two warps: warp 8 issues the QK chunks, warp 9 the V
+      // chunks, each in ring order.  One thread alone keeps the tensor cores
+      // about half busy (its barrier waits and commits cannot overlap its own
+      // MMAs); two interleave.  Each stream has its own "full" barrier per slot,
+      // so a barrier phase is never awaited while an earlier phase of the other
+      // stream in that slot is still open.  The waits are compiled in (a call
+      // here costs more than the four MMAs of a chunk) and CTA-scoped: the data
+      // they publish is read by the tensor cores, not by this thread.
+      const bool v_issuer = warp != SA_MMA_WARP;
+      bool ok = mbar_wait(&sh->q_full, 0, wc) && mbar_wait(&sh->peer_q, 0, wc, true);
+      // Descriptors are built once; a byte offset o moves the start address field by o / 16.
+      const uint64_t rd0 = sdesc_sw128(smem_u32(smem + p.r_off), v_issuer ? SA_VSEG : 16, 1024);
+      uint32_t ph = 0;  // bit k: parity of the next phase of slot k's full barrier for this stream
+      // ring position of (block j, chunk c) of this stream
+      auto pos = [&](int j, int c) -> uint32_t {
+        if (!v_issuer) return j == 0 ? (uint32_t)c : (uint32_t)(nkb + (j - 1) * (nkb + SA_NKC) + c);
+        return (uint32_t)(nkb + j * (nkb + SA_NKC) + (j + 1 < p.nblk ? nkb : 0) + c);
+      };
+      // Chunks are taken two at a time (ring positions n, n + 1): both barriers
+      // are probed before either result is needed, so one probe latency covers
+      // eight MMAs.
+      uint64_t* const fulls = v_issuer ? sh->full_v : sh->full_s;
+      auto take2 = [&](uint32_t n, bool two, int& s0, int& s1) -> bool {
+        s0 = (int)(n % (uint32_t)p.n_slots);
+        s1 = s0 + 1 == p.n_slots ? 0 : s0 + 1;
+        const uint32_t b0 = smem_u32(&fulls[s0]), b1 = smem_u32(&fulls[s1]);
+        const uint32_t q0 = (ph >> s0) & 1u, q1 = (ph >> s1) & 1u;
+        bool r0 = mbar_poll(b0, q0);
+        bool r1 = !two || mbar_poll(b1, q1);
+        if (!r0) r0 = mbar_wait_inl(&fulls[s0], q0, wc);
+        if (r0 && !r1) r1 = mbar_wait_inl(&fulls[s1], q1, wc);
+        ph ^= (1u << s0) | (two ? 1u << s1 : 0u);
+        tc_fence_after();
+        return r0 && r1;
+      };
+      if (!v_issuer) {
+        const uint64_t qd0 = sdesc_sw128(smem_u32(qs), 16, 1024);
+        const uint32_t idesc_s = idesc_bf16_f32(128, SA_NB, false, false);
+        for (int j = 0; ok && j < p.nblk; ++j) {
+          // S buffer j % 2 was last read by softmax(j - 2)
+          if (j >= 2 && !(ok = mbar_wait_inl(&sh->s_free[j & 1], ((j - 2) >> 1) & 1, wc))) break;
+          const uint32_t d_s = tmem + (j & 1) * SA_SCOLS;
+          for (int d = 0; d < nkb; d += 2) {
+            const uint32_t n = pos(j, d);
+            const bool two = d + 1 < nkb;
+            int sl[2];
+            if (!(ok = take2(n, two, sl[0], sl[1]))) break;
+            for (int h = 0; h < (two ? 2 : 1); ++h) {
+              const uint64_t boff = (uint64_t)(sl[h] * (SA_SLOT >> 4));
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                umma_bf16_ss_cg2(d_s, qd0 + (uint64_t)((d + h) * 512 + kk * 2), rd0 + boff + (uint64_t)(kk * 2),
+                                 idesc_s, (d + h > 0 || kk > 0) ? 1u : 0u);
+              umma_commit_cg2(&sh->empty[sl[h]], 3);
+              KS_SA_TRACE(12, n + h);
             }
-            umma_commit_cg2(&sh->s_empty[slot], 3);
           }
           if (!ok) break;
           umma_commit_cg2(&sh->acc_full[j & 1], 3);
         }
-        if (j >= 1) {
-          const int jj = j - 1;
-          if (!(ok = mbar_wait(&sh->p_full, jj & 1, wc) &&
-                     mbar_wait(&sh->peer_p_full, jj & 1, wc, true)))
-            break;
-          for (int kc = 0; kc < SA_NKC; ++kc, ++vc) {
-            const int slot = vc % p.nv_slots;
-            const uint32_t ph = (vc / p.nv_slots) & 1;
-            if (!(ok = mbar_wait(&sh->v_full[slot], ph, wc) &&
-                       mbar_wait(&sh->peer_v_full[slot], ph, wc, true)))
-              break;
-            tc_fence_after();
-            fence_proxy_async_smem();
-            const uint32_t vaddr = smem_u32(smem + p.v_off + slot * p.v_bytes);
-            uint32_t ocol = tmem + SA_OCOL;
-            int u = 0;
-            for (int i = 0; i < p.n_pv; ++i) {
-              const uint32_t idesc_pv = idesc_bf16_f32(128, p.pv_n[i], false, true);
+        umma_commit_cg2(&sh->drain_s, 1);
+        mbar_wait(&sh->drain_s, 0, wc, false, true);
+      } else {
+        const uint64_t pd0 = sdesc_sw128(smem_u32(ps), 16, 1024);
+        uint32_t idesc_pv[2];
+        for (int i = 0; i < p.n_pv; ++i) idesc_pv[i] = idesc_bf16_f32(128, p.pv_n[i], false, true);
+        for (int j = 0; ok && j < p.nblk; ++j) {
+          // P(j) written (and O rescaled) by the softmax
+          if (!(ok = mbar_wait_inl(&sh->p_full, j & 1, wc))) break;
+          KS_SA_TRACE(8, j);
+          for (int sp = 0; sp < SA_NKC; sp += 2) {
+            const uint32_t n = pos(j, sp);
+            int sl[2];
+            if (!(ok = take2(n, true, sl[0], sl[1]))) break;
 #pragma unroll
-              for (int kk = 0; kk < SA_KC / 16; ++kk) {
-                const uint64_t ad = sdesc_sw128(paddr + kc * 8192 + kk * 32, 16, 1024);
-                const uint64_t bd = sdesc_sw128(vaddr + u * 8192 + kk * 2048, 8192, 1024);
-                umma_bf16_ss_cg2(ocol, ad, bd, idesc_pv, (jj > 0 || kc > 0 || kk > 0) ? 1u : 0u);
+            for (int h = 0; h < 2; ++h) {
+              const int sub = sp + h;
+              const uint64_t boff = (uint64_t)(sl[h] * (SA_SLOT >> 4));
+              uint32_t ocol = tmem + SA_OCOL;
+              int sg = 0;
+              for (int i = 0; i < p.n_pv; ++i) {
+#pragma unroll
+                for (int kk = 0; kk < SA_KC / 16; ++kk)
+                  umma_bf16_ss_cg2(ocol, pd0 + (uint64_t)((sub >> 1) * 512 + ((sub & 1) * 2 + kk) * 2),
+                                   rd0 + boff + (uint64_t)(sg * (SA_VSEG >> 4) + kk * 128), idesc_pv[i],
+                                   (j > 0 || sub > 0 || kk > 0) ? 1u : 0u);
+                ocol += p.pv_n[i] / 2;
+                sg += p.pv_n[i] / 128;
               }
-              ocol += p.pv_n[i] / 2;
-              u += p.pv_n[i] / 128;
+              umma_commit_cg2(&sh->empty[sl[h]], 3);
+              KS_SA_TRACE(12, n + h);
             }
-            umma_commit_cg2(&sh->v_empty[slot], 3);
           }
           if (!ok) break;
           umma_commit_cg2(&sh->p_free, 3);
         }
+        if (ok) umma_commit_cg2(&sh->o_full, 3);
+        umma_commit_cg2(&sh->drain_v, 1);
+        mbar_wait(&sh->drain_v, 0, wc, false, true);
       }
-      if (ok) umma_commit_cg2(&sh->o_full, 3);
-      umma_commit_cg2(&sh->drain, 1);
-      mbar_wait(&sh->drain, 0, wc, false, true);
-    } else if (lane == 0) {
-      // ---------------------------------------------------------- relay (CTA 1)
-      // Forwards "my QK chunk landed", "my P is written" and "my V chunk landed"
-      // to the leader CTA, in the leader's consumption order.
-      bool ok = mbar_wait(&sh->q_full, 0, wc);
-      if (ok) mbar_arrive_cluster(&sh->peer_q, 0);
-      uint32_t sc = 0, vc = 0;
-      for (int j = 0; ok && j <= p.nblk; ++j) {
-        if (j < p.nblk) {
-          for (int d = 0; d < nkb; ++d, ++sc) {
-            if (!(ok = mbar_wait(&sh->s_full[sc % p.ns_slots], (sc / p.ns_slots) & 1, wc))) break;
-            mbar_arrive_cluster(&sh->peer_s_full[sc % p.ns_slots], 0);
-          }
-          if (!ok) break;
-        }
-        if (j >= 1) {
-          if (!(ok = mbar_wait(&sh->p_full, (j - 1) & 1, wc))) break;
-          mbar_arrive_cluster(&sh->peer_p_full, 0);
-          for (int kc = 0; kc < SA_NKC; ++kc, ++vc) {
-            if (!(ok = mbar_wait(&sh->v_full[vc % p.nv_slots], (vc / p.nv_slots) & 1, wc))) break;
-            mbar_arrive_cluster(&sh->peer_v_full[vc % p.nv_slots], 0);
-          }
-        }
-      }
+    } else if (lane == 0 && warp == SA_MMA_WARP) {
+      // CTA 1: tell the leader that this CTA's query tile has landed
+      if (mbar_wait(&sh->q_full, 0, wc)) mbar_arrive_cluster(&sh->peer_q, 0);
     }
   } else if (warp >= SA_SMX_WARP0) {
     // ------------------------------------------------------------ softmax + epilogue
@@ -353,7 +402,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
     float m_used = sink2, lsum = 0.f;
     const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
     const int o_cols = p.dv_pad / 2;
-    const int32_t* ip = p.idx + token * p.K;
     // validity bits of this lane's 128 keys of block j (warp-uniform loads)
     auto valid_bits = [&](int j, uint32_t* mk) {
       const int k0 = j * SA_NB + half * SA_HALF;
@@ -386,9 +434,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       const int sb = j & 1;
       uint32_t mk[4];
       valid_bits(j, mk);
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->acc_full[sb], (j >> 1) & 1, wc));
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->acc_full[sb], (j >> 1) & 1, wc));
       if (!ok) break;
       tc_fence_after();
+      if (l == 0) KS_SA_TRACE(9, j);
       const uint32_t sbase = lane_base + sb * SA_SCOLS;
       // pass 1: block max over this lane's 128 keys
       float bmax = -INFINITY;
@@ -404,7 +453,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       // block max of the head = max over this lane and its partner (lane l ^ 64)
       sh->xslot[j & 1][l] = bmax;
       mbar_arrive(&sh->xchg[j & 1]);
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->xchg[j & 1], (j >> 1) & 1, wc));
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->xchg[j & 1], (j >> 1) & 1, wc));
       if (!ok) break;
       const float m_new = fmaxf(m_used, fmaxf(bmax, sh->xslot[j & 1][l ^ 64]));
       const bool resc = m_new > m_used + 8.f;
@@ -416,7 +465,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       }
       if (j >= 1) {
         // P buffer free and O stable: PV of block j-1 done
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->p_free, (j - 1) & 1, wc));
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->p_free, (j - 1) & 1, wc));
         if (!ok) break;
         if (__any_sync(0xFFFFFFFFu, resc)) {  // TMEM access is warp-wide; alpha = 1 elsewhere
           tc_fence_after();
@@ -431,6 +480,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
           tmem_wait_st();
         }
       }
+      if (l == 0) KS_SA_TRACE(10, j);
       // pass 2: probabilities as bf16, straight into P row m, keys [128*half, +128)
       // (64-key blocks 2*half and 2*half + 1; 32 keys = four 16-byte chunks per step)
 #pragma unroll
@@ -455,9 +505,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
-      fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&sh->p_full);
+      sa_warp_ready(&sh->p_full, cta, lane);
+      if (lane == 0) {  // S buffer sb read out
+        if (cta == 0) mbar_arrive(&sh->s_free[sb]);
+        else mbar_arrive_cluster(&sh->s_free[sb], 0);
+      }
+      if (lane == 0) KS_SA_TRACE(11, 16 * q4 + j);
     }
     if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->o_full, 0, wc));
     if (ok) {
