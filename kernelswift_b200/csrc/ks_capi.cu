@@ -291,7 +291,7 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
   const uint32_t nkb = (uint32_t)(D / 64);
   p.q_off = SA_HDR;
   p.p_off = p.q_off + nkb * 8192;
-  p.r_off = p.p_off + SA_PBYTES;
+  p.r_off = p.p_off + 2 * SA_PBYTES;  // P double buffered
   // ring: as many 16 KB slots as fit in the 227 KB per-CTA limit
   const size_t limit = 232448 - 1024 /* alignment slack */;
   const size_t avail = limit > p.r_off ? limit - p.r_off : 0;

@@ -101,7 +101,9 @@ struct SaParams {
 struct SaShared {
   uint64_t full_s[SA_MAX_SLOTS], full_v[SA_MAX_SLOTS], empty[SA_MAX_SLOTS];
   uint64_t acc_full[2], s_free[2];
-  uint64_t p_full, p_free, o_full, q_full, peer_q, drain_s, drain_v;
+  // per P buffer: with two buffers the softmax can finish P(j + 1) before the V
+  // issuer has seen P(j), so one barrier would run two phases ahead of its waiter
+  uint64_t p_full[2], p_free[2], o_full, q_full, peer_q, drain_s, drain_v;
   uint64_t xchg[3];
   uint32_t tmem_base;
   int abort;
@@ -154,8 +156,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
     mbar_init(&sh->acc_full[1], 1);
     mbar_init(&sh->s_free[0], 2 * SA_SMX_WARPS);
     mbar_init(&sh->s_free[1], 2 * SA_SMX_WARPS);
-    mbar_init(&sh->p_full, 2 * SA_SMX_WARPS);
-    mbar_init(&sh->p_free, 1);
+    mbar_init(&sh->p_full[0], 2 * SA_SMX_WARPS);
+    mbar_init(&sh->p_full[1], 2 * SA_SMX_WARPS);
+    mbar_init(&sh->p_free[0], 1);
+    mbar_init(&sh->p_free[1], 1);
     mbar_init(&sh->o_full, 1);
     mbar_init(&sh->q_full, 1);  // TMA of the query tile
     mbar_init(&sh->peer_q, 1);
@@ -332,15 +336,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
           for (int d = 0; d < nkb; d += 2) {
             const uint32_t n = pos(j, d);
             const bool two = d + 1 < nkb;
-            int sl[2];
-            if (!(ok = take2(n, two, sl[0], sl[1]))) break;
-            for (int h = 0; h < (two ? 2 : 1); ++h) {
-              const uint64_t boff = (uint64_t)(sl[h] * (SA_SLOT >> 4));
+            int sl0, sl1;
+            if (!(ok = take2(n, two, sl0, sl1))) break;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (h == 1 && !two) break;
+              const int slh = h ? sl1 : sl0;
+              const uint64_t boff = (uint64_t)(slh * (SA_SLOT >> 4));
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
                 umma_bf16_ss_cg2(d_s, qd0 + (uint64_t)((d + h) * 512 + kk * 2), rd0 + boff + (uint64_t)(kk * 2),
                                  idesc_s, (d + h > 0 || kk > 0) ? 1u : 0u);
-              umma_commit_cg2(&sh->empty[sl[h]], 3);
+              umma_commit_cg2(&sh->empty[slh], 3);
               KS_SA_TRACE(12, n + h);
             }
           }
@@ -351,37 +358,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         mbar_wait(&sh->drain_s, 0, wc, false, true);
       } else {
         const uint64_t pd0 = sdesc_sw128(smem_u32(ps), 16, 1024);
-        uint32_t idesc_pv[2];
-        for (int i = 0; i < p.n_pv; ++i) idesc_pv[i] = idesc_bf16_f32(128, p.pv_n[i], false, true);
+        // (scalars, not arrays: an array indexed in a loop would live in local memory)
+        const uint32_t idesc_pv0 = idesc_bf16_f32(128, p.pv_n[0], false, true);
+        const uint32_t idesc_pv1 = idesc_bf16_f32(128, p.n_pv > 1 ? p.pv_n[1] : 128, false, true);
+        const int npv = p.n_pv, pvn0 = p.pv_n[0];
         for (int j = 0; ok && j < p.nblk; ++j) {
           // P(j) written (and O rescaled) by the softmax
-          if (!(ok = mbar_wait_inl(&sh->p_full, j & 1, wc))) break;
+          if (!(ok = mbar_wait_inl(&sh->p_full[j & 1], (j >> 1) & 1, wc))) break;
           KS_SA_TRACE(8, j);
           for (int sp = 0; sp < SA_NKC; sp += 2) {
             const uint32_t n = pos(j, sp);
-            int sl[2];
-            if (!(ok = take2(n, true, sl[0], sl[1]))) break;
+            int sl0, sl1;
+            if (!(ok = take2(n, true, sl0, sl1))) break;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int sub = sp + h;
-              const uint64_t boff = (uint64_t)(sl[h] * (SA_SLOT >> 4));
-              uint32_t ocol = tmem + SA_OCOL;
-              int sg = 0;
-              for (int i = 0; i < p.n_pv; ++i) {
+              const int slh = h ? sl1 : sl0;
+              const uint64_t boff = (uint64_t)(slh * (SA_SLOT >> 4));
+              const uint64_t ad = pd0 + (uint64_t)((j & 1) * (SA_PBYTES >> 4) + (sub >> 1) * 512 + (sub & 1) * 4);
+#pragma unroll
+              for (int i = 0; i < 2; ++i) {
+                if (i == 1 && npv < 2) break;
+                // instruction i: N = pv_n[i]; its columns start at segment 2 i (pv_n[0] = 256 when there are two)
+                const uint32_t ocol = tmem + SA_OCOL + (i ? pvn0 / 2 : 0);
+                const uint64_t bd = rd0 + boff + (uint64_t)(i ? (pvn0 / 128) * (SA_VSEG >> 4) : 0);
 #pragma unroll
                 for (int kk = 0; kk < SA_KC / 16; ++kk)
-                  umma_bf16_ss_cg2(ocol, pd0 + (uint64_t)((sub >> 1) * 512 + ((sub & 1) * 2 + kk) * 2),
-                                   rd0 + boff + (uint64_t)(sg * (SA_VSEG >> 4) + kk * 128), idesc_pv[i],
+                  umma_bf16_ss_cg2(ocol, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 128), i ? idesc_pv1 : idesc_pv0,
                                    (j > 0 || sub > 0 || kk > 0) ? 1u : 0u);
-                ocol += p.pv_n[i] / 2;
-                sg += p.pv_n[i] / 128;
               }
-              umma_commit_cg2(&sh->empty[sl[h]], 3);
+              umma_commit_cg2(&sh->empty[slh], 3);
               KS_SA_TRACE(12, n + h);
             }
           }
           if (!ok) break;
-          umma_commit_cg2(&sh->p_free, 3);
+          umma_commit_cg2(&sh->p_free[j & 1], 3);
         }
         if (ok) umma_commit_cg2(&sh->o_full, 3);
         umma_commit_cg2(&sh->drain_v, 1);
@@ -439,17 +450,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       tc_fence_after();
       if (l == 0) KS_SA_TRACE(9, j);
       const uint32_t sbase = lane_base + sb * SA_SCOLS;
-      // pass 1: block max over this lane's 128 keys
+      // pass 1: block max over this lane's 128 keys of s * scale, taken over the raw
+      // scores s * sign(scale) and scaled once (rounding is monotonic)
+      const float sgn = p.scale_log2 < 0.f ? -1.f : 1.f;
       float bmax = -INFINITY;
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
         uint32_t r[32];
         tmem_ld32(sbase + 32 * w, r);
         tmem_wait_ld();
+        float m0 = -INFINITY, m1 = -INFINITY;
+        if (mk[w] == 0xFFFFFFFFu) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if ((mk[w] >> i) & 1u) bmax = fmaxf(bmax, __uint_as_float(r[i]) * p.scale_log2);
+          for (int i = 0; i < 32; i += 2) {
+            m0 = fmaxf(m0, sgn * __uint_as_float(r[i]));
+            m1 = fmaxf(m1, sgn * __uint_as_float(r[i + 1]));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            m0 = fmaxf(m0, ((mk[w] >> i) & 1u) ? sgn * __uint_as_float(r[i]) : -INFINITY);
+            m1 = fmaxf(m1, ((mk[w] >> (i + 1)) & 1u) ? sgn * __uint_as_float(r[i + 1]) : -INFINITY);
+          }
+        }
+        bmax = fmaxf(bmax, fmaxf(m0, m1));
       }
+      bmax = (sgn * bmax) * p.scale_log2;  // -inf when no key is valid
       // block max of the head = max over this lane and its partner (lane l ^ 64)
       sh->xslot[j & 1][l] = bmax;
       mbar_arrive(&sh->xchg[j & 1]);
@@ -463,11 +489,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         lsum *= alpha;
         m_used = m_new;
       }
-      if (j >= 1) {
-        // P buffer free and O stable: PV of block j-1 done
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->p_free, (j - 1) & 1, wc));
+      // P is double buffered: P(j) goes to buffer j % 2, last read by PV(j - 2)
+      if (j >= 2) {
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->p_free[j & 1], ((j - 2) >> 1) & 1, wc));
         if (!ok) break;
-        if (__any_sync(0xFFFFFFFFu, resc)) {  // TMEM access is warp-wide; alpha = 1 elsewhere
+      }
+      if (j >= 1 && __any_sync(0xFFFFFFFFu, resc)) {  // TMEM access is warp-wide; alpha = 1 elsewhere
+        // O is rescaled once PV(j - 1) has finished with it
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, wc));
+        if (!ok) break;
+        {
           tc_fence_after();
           for (int c = 0; c < o_cols; c += 16) {
             uint32_t o[16];
@@ -482,31 +513,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       }
       if (l == 0) KS_SA_TRACE(10, j);
       // pass 2: probabilities as bf16, straight into P row m, keys [128*half, +128)
-      // (64-key blocks 2*half and 2*half + 1; 32 keys = four 16-byte chunks per step)
+      // (64-key blocks 2*half and 2*half + 1; 16 keys = two 16-byte chunks per step):
+      // p = 2^(s * scale_log2 - m), one FFMA and one ex2 per score; masked keys -> 0.
+      {
+        const float neg_m = -m_used;
+        float ls0 = 0.f, ls1 = 0.f;
+        uint8_t* pbase = ps + (j & 1) * SA_PBYTES + (2 * half) * 8192 + m * 128;
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        uint32_t r[32];
-        tmem_ld32(sbase + 32 * w, r);
-        tmem_wait_ld();
-        uint32_t pk[16];
+        for (int c16 = 0; c16 < 8; ++c16) {
+          uint32_t r[16];
+          tmem_ld16(sbase + 16 * c16, r);
+          tmem_wait_ld();
+          const uint32_t bits = (mk[c16 >> 1] >> ((c16 & 1) * 16)) & 0xFFFFu;
+          uint32_t pk[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float s0 = ((mk[w] >> (2 * i)) & 1u) ? __uint_as_float(r[2 * i]) * p.scale_log2 : -INFINITY;
-          const float s1 = ((mk[w] >> (2 * i + 1)) & 1u) ? __uint_as_float(r[2 * i + 1]) * p.scale_log2 : -INFINITY;
-          const float e0 = ex2f(s0 - m_used), e1 = ex2f(s1 - m_used);
-          lsum += e0 + e1;
-          pk[i] = cvt_bf16x2(e0, e1);
+          for (int i = 0; i < 8; ++i) {
+            float e0 = ex2f(fmaf(__uint_as_float(r[2 * i]), p.scale_log2, neg_m));
+            float e1 = ex2f(fmaf(__uint_as_float(r[2 * i + 1]), p.scale_log2, neg_m));
+            if (bits != 0xFFFFu) {
+              e0 = ((bits >> (2 * i)) & 1u) ? e0 : 0.f;
+              e1 = ((bits >> (2 * i + 1)) & 1u) ? e1 : 0.f;
+            }
+            ls0 += e0;
+            ls1 += e1;
+            pk[i] = cvt_bf16x2(e0, e1);
+          }
+          // keys 16 c16 .. +16 of this half: 64-key block c16 / 4, 16-byte chunks 2 (c16 % 4) + {0, 1}
+          uint8_t* prow = pbase + (c16 >> 2) * 8192;
+          const int cc = (c16 & 3) * 2;
+          *reinterpret_cast<uint4*>(prow + ((cc ^ (m & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(prow + (((cc + 1) ^ (m & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
-        uint8_t* prow = ps + (2 * half + (w >> 1)) * 8192 + m * 128;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int cc = (w & 1) * 4 + q;
-          *reinterpret_cast<uint4*>(prow + ((cc ^ (m & 7)) << 4)) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-        }
+        lsum += ls0 + ls1;
       }
       tc_fence_before();
-      sa_warp_ready(&sh->p_full, cta, lane);
+      sa_warp_ready(&sh->p_full[j & 1], cta, lane);
       if (lane == 0) {  // S buffer sb read out
         if (cta == 0) mbar_arrive(&sh->s_free[sb]);
         else mbar_arrive_cluster(&sh->s_free[sb], 0);
