@@ -18,8 +18,9 @@
 
 namespace ks {
 
-// Per-device status word written by kernels whose bounded waits ran out.
-__device__ int g_status_word;
+// Per-device status written by kernels whose bounded waits ran out: [0] the code,
+// [1], [2] where the first timeout happened (block; thread, barrier offset, parity).
+__device__ int g_status_word[4];
 
 namespace {
 
@@ -468,15 +469,19 @@ int ks_device_status(void* stream) {
   if (int rc = device(&dev)) return rc;
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
-  int v = 0;
-  e = cudaMemcpy(&v, dev->status, sizeof(int), cudaMemcpyDeviceToHost);
+  int v[4] = {0, 0, 0, 0};
+  e = cudaMemcpy(v, dev->status, sizeof(v), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "read status word");
-  if (v != 0) {
-    const int zero = 0;
-    e = cudaMemcpy(dev->status, &zero, sizeof(int), cudaMemcpyHostToDevice);
+  if (v[0] != 0) {
+    const int zero[4] = {0, 0, 0, 0};
+    e = cudaMemcpy(dev->status, zero, sizeof(zero), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_fail(e, "clear status word");
-    return fail(KS_ERR_DEVICE, "device status %d (%s)", v,
-                v == DEV_TIMEOUT ? "a bounded wait timed out" : "bounds check failed");
+    if (v[0] == DEV_TIMEOUT)
+      return fail(KS_ERR_DEVICE,
+                  "device status %d (a bounded wait timed out: block %d, thread %d, barrier at "
+                  "shared offset %d, parity %d, tag %d)",
+                  v[0], v[1], (int)((unsigned)v[2] >> 20), (v[2] >> 1) & 0x7FFFF, v[2] & 1, v[3]);
+    return fail(KS_ERR_DEVICE, "device status %d (bounds check failed)", v[0]);
   }
   return KS_OK;
 }

@@ -87,30 +87,6 @@ __device__ __forceinline__ bool mbar_test_cluster(uint32_t bar, uint32_t parity)
   return ok != 0;
 }
 
-// try_wait that may suspend the thread for up to `hint_ns` (or until the phase
-// completes): a waiting warp sleeps instead of spinning, so it takes no issue
-// slots from the warps that share its scheduler.
-__device__ __forceinline__ bool mbar_test_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_test_sleep_cluster(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;"
-      " selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-constexpr uint32_t kSleepHintNs = 20000;
-
 // Non-blocking probes (mbarrier.test_wait): for loops that poll several barriers;
 // try_wait may suspend the thread on the first incomplete barrier it probes.
 __device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity) {
@@ -137,8 +113,9 @@ __device__ __forceinline__ bool mbar_poll_cluster(uint32_t bar, uint32_t parity)
 // memory), the global status word and the time budget of one wait.
 struct WaitCtx {
   volatile int* abort;  // shared memory
-  int* status;          // global memory, may be null
+  int* status;          // global memory (4 ints: code and where the first timeout was), may be null
   uint64_t budget_ns;
+  int tag = 0;          // caller's progress marker, reported with a timeout
 };
 
 // Budgets are enforced with the SM cycle counter (cheap to read, unlike
@@ -150,6 +127,17 @@ __device__ __forceinline__ uint64_t budget_cycles(uint64_t budget_ns) { return b
 __device__ __forceinline__ void raise_error(const WaitCtx& w, int code) {
   *w.abort = 1;
   if (w.status) atomicCAS(w.status, 0, code);
+}
+// A timed-out wait also records where it happened (first one only):
+// status[1] = block, status[2] = thread << 20 | barrier's shared-memory offset << 1 | parity,
+// status[3] = the waiting thread's progress tag.
+__device__ __forceinline__ void raise_timeout(const WaitCtx& w, uint32_t bar, uint32_t parity) {
+  *w.abort = 1;
+  if (w.status && atomicCAS(w.status, 0, DEV_TIMEOUT) == 0) {
+    w.status[1] = (int)blockIdx.x;
+    w.status[2] = (int)((threadIdx.x << 20) | ((bar & 0x7FFFFu) << 1) | (parity & 1u));
+    w.status[3] = w.tag;
+  }
 }
 
 // Wait until the phase with `parity` of `bar` completes.  Returns false when the
@@ -164,12 +152,12 @@ __device__ __forceinline__ bool mbar_wait_body(uint64_t* bar, uint32_t parity, c
   const uint64_t t0 = clock64();
   const uint64_t lim = budget_cycles(w.budget_ns);
   for (;;) {
-    if (cluster_scope ? mbar_test_sleep_cluster(b, parity, kSleepHintNs)
-                      : mbar_test_sleep(b, parity, kSleepHintNs))
-      return true;
+    // try_wait without a suspend-time hint: with a hint, a waiting thread was seen
+    // (rarely) never to return although the phase had completed.
+    if (cluster_scope ? mbar_test_cluster(b, parity) : mbar_test(b, parity)) return true;
     if (!drain && *w.abort) return false;
     if ((uint64_t)clock64() - t0 > lim) {
-      raise_error(w, DEV_TIMEOUT);
+      raise_timeout(w, b, parity);
       return false;
     }
   }

@@ -268,6 +268,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       }
       fetch(n + SA_GROUPS);
       const int slot = (int)(n % (uint32_t)p.n_slots);
+      wc.tag = (int)n;
       if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->empty[slot], ((n / p.n_slots) & 1) ^ 1, wc))))
         break;
       if (u == 0) KS_SA_TRACE(g, n / SA_GROUPS);
@@ -287,7 +288,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       sa_warp_ready(is_v ? &sh->full_v[slot] : &sh->full_s[slot], cta, lane);
       if (u == 0) KS_SA_TRACE(4 + g, n / SA_GROUPS);
     }
-    if (threadIdx.x == 0) mbar_wait(&sh->q_full, 0, wc, false, true);
+    if (threadIdx.x == 0) {
+      mbar_wait(&sh->q_full, 0, wc, false, true);
+      // Tail: the tensor cores signal "slot consumed" asynchronously, also into
+      // this CTA from the leader's commits.  Wait until the last signal of every
+      // slot has landed, so none can reach the barriers of the next CTA that
+      // this SM runs.
+      // (Skipped after an abort: the waits would only run out their budgets.)
+      for (int sl = 0; sl < p.n_slots && !*wc.abort; ++sl) {
+        const uint32_t uses = (n_total + (uint32_t)(p.n_slots - 1 - sl)) / (uint32_t)p.n_slots;
+        if (uses > 0) mbar_wait(&sh->empty[sl], (uses - 1) & 1, wc, false, true);
+      }
+    }
   } else if (warp == SA_MMA_WARP || warp == SA_MMA_WARP + 1) {
     if (lane == 0 && cta == 0) {
       // ---------------------------------------------------------- MMA issuers (leader CTA)
@@ -314,6 +326,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       // eight MMAs.
       uint64_t* const fulls = v_issuer ? sh->full_v : sh->full_s;
       auto take2 = [&](uint32_t n, bool two, int& s0, int& s1) -> bool {
+        wc.tag = (int)n;
         s0 = (int)(n % (uint32_t)p.n_slots);
         s1 = s0 + 1 == p.n_slots ? 0 : s0 + 1;
         const uint32_t b0 = smem_u32(&fulls[s0]), b1 = smem_u32(&fulls[s1]);
@@ -331,6 +344,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         const uint32_t idesc_s = idesc_bf16_f32(128, SA_NB, false, false);
         for (int j = 0; ok && j < p.nblk; ++j) {
           // S buffer j % 2 was last read by softmax(j - 2)
+          wc.tag = 2000 + j;
           if (j >= 2 && !(ok = mbar_wait_inl(&sh->s_free[j & 1], ((j - 2) >> 1) & 1, wc))) break;
           const uint32_t d_s = tmem + (j & 1) * SA_SCOLS;
           for (int d = 0; d < nkb; d += 2) {
@@ -364,6 +378,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         const int npv = p.n_pv, pvn0 = p.pv_n[0];
         for (int j = 0; ok && j < p.nblk; ++j) {
           // P(j) written (and O rescaled) by the softmax
+          wc.tag = 1000 + j;
           if (!(ok = mbar_wait_inl(&sh->p_full[j & 1], (j >> 1) & 1, wc))) break;
           KS_SA_TRACE(8, j);
           for (int sp = 0; sp < SA_NKC; sp += 2) {
@@ -445,6 +460,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       const int sb = j & 1;
       uint32_t mk[4];
       valid_bits(j, mk);
+      wc.tag = 3000 + j;
       ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->acc_full[sb], (j >> 1) & 1, wc));
       if (!ok) break;
       tc_fence_after();
@@ -555,6 +571,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       if (lane == 0) KS_SA_TRACE(11, 16 * q4 + j);
     }
     if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->o_full, 0, wc));
+    // tail: the last two "P free" signals land before the CTA exits (see the gathers)
+    for (int jj = p.nblk - 2; ok && jj < p.nblk; ++jj)
+      if (jj >= 0) mbar_wait(&sh->p_free[jj & 1], (jj >> 1) & 1, wc, false, true);
     if (ok) {
       sh->xslot[2][l] = lsum;
       mbar_arrive(&sh->xchg[2]);
