@@ -207,6 +207,18 @@ int indexer_scores_impl(const void* q, const void* k, int64_t k_batch_rows, cons
   }
 }
 
+template <int EPT>
+int launch_topk(const TopkParams& p, int64_t rows, size_t smem, cudaStream_t st) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(topk_rows_kernel<EPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(topk)");
+  topk_rows_kernel<EPT><<<(unsigned)rows, TK_THREADS, smem, st>>>(p);
+  return launch_check("topk_rows_kernel launch");
+}
+
 int topk_impl(const void* scores, int64_t score_ld, int64_t B, int64_t S, int64_t T,
               int64_t pos0, int32_t causal, int32_t ratio, int32_t topk, int64_t offset,
               void* out, int32_t out_dtype, cudaStream_t st) {
@@ -240,16 +252,16 @@ int topk_impl(const void* scores, int64_t score_ld, int64_t B, int64_t S, int64_
   p.out_row_stride = K;
   p.kpow2 = kpow2;
   p.status = dev->status;
-  const size_t smem = (size_t)kpow2 * 4 + (256 + 256 + TK_WARPS + 4 + 8) * 4 + round_up(T, 8) * 2;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
-  });
-  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(topk)");
   if (B * S > 0x7FFFFFFFll) return fail(KS_ERR_UNSUPPORTED, "topk: too many rows");
-  topk_rows_kernel<<<(unsigned)(B * S), TK_THREADS, smem, st>>>(p);
-  return launch_check("topk_rows_kernel launch");
+  // composites sorted per row: TK_THREADS * ept >= kpow2
+  const int ept = kpow2 <= TK_THREADS ? 1 : kpow2 / TK_THREADS;
+  const size_t smem = (size_t)TK_THREADS * ept * 4 + (256 + 256 + TK_WARPS + 4 + 8) * 4 + round_up(T, 8) * 2;
+  switch (ept) {
+    case 1: return launch_topk<1>(p, B * S, smem, st);
+    case 2: return launch_topk<2>(p, B * S, smem, st);
+    case 4: return launch_topk<4>(p, B * S, smem, st);
+    default: return launch_topk<8>(p, B * S, smem, st);
+  }
 }
 
 int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int32_t* idx,

@@ -10,15 +10,19 @@
 //
 // One CTA per row.  The valid prefix of the row is staged once in shared memory
 // as 16-bit order keys (monotone in the bf16 value, -0.0 folded onto +0.0).
-//   1. histogram of the high key byte (warp-aggregated shared atomics) and a
-//      suffix scan find the byte of the k-th largest key; a second histogram over
-//      the low byte of that bucket gives the exact threshold key `thr`, the count
-//      of keys above it and how many keys equal to it are taken (lowest indices
-//      first);
-//   2. one pass in index order compacts the selected (key, index) pairs with two
-//      block-wide exclusive scans per 4096-element chunk;
+//   1. histogram of the high key byte (shared atomics) and a suffix scan find the
+//      byte of the k-th largest key; a second histogram over the low byte, fed
+//      only by the keys of that bucket, gives the exact threshold key `thr`, the
+//      count of keys above it and how many keys equal to it are taken (lowest
+//      indices first);
+//   2. one pass in index order compacts the selected (key, index) pairs with one
+//      block-wide exclusive scan per 4096-element chunk (counts of keys above and
+//      equal to `thr` packed into one word);
 //   3. a bitonic sort of the 32-bit composites ((0xFFFF-key)<<16 | index) puts
-//      them in (value desc, index asc) order; the composites are all distinct;
+//      them in (value desc, index asc) order; the composites are all distinct.
+//      Each thread holds EPT consecutive composites in registers: strides below
+//      EPT are exchanged in registers, strides within a warp by shuffles, and only
+//      the strides across warps go through shared memory;
 //   4. the post-processed indices are written as int64 or int32.
 #pragma once
 #include "ks_device.cuh"
@@ -49,14 +53,6 @@ __device__ __forceinline__ uint32_t bf16_key(uint32_t u) {
   u &= 0xFFFFu;
   if (u == 0x8000u) u = 0;  // -0.0 == +0.0
   return (u & 0x8000u) ? ((~u) & 0xFFFFu) : (u | 0x8000u);
-}
-
-__device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool pred) {
-  const uint32_t active = __ballot_sync(0xFFFFFFFFu, pred);
-  if (pred) {
-    const uint32_t peers = __match_any_sync(active, bin);
-    if ((threadIdx.x & 31) == (uint32_t)(__ffs(peers) - 1)) atomicAdd(hist + bin, __popc(peers));
-  }
 }
 
 // Exclusive scan of one value per thread over the block; also returns the total.
@@ -114,11 +110,13 @@ __device__ __forceinline__ void find_bin(const uint32_t* hist, uint32_t need, ui
   __syncthreads();
 }
 
+template <int EPT>
 __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
+  constexpr int NS = TK_THREADS * EPT;  // sorted composites, >= kpow2
   extern __shared__ __align__(16) uint8_t tk_smem[];
-  // layout: sortbuf[kpow2] u32 | hist[256] | scan[256] | warp_tot[TK_WARPS+1] | misc[8] | keys
+  // layout: sortbuf[NS] u32 | hist[256] | scan[256] | warp_tot[TK_WARPS+4] | misc[8] | keys
   uint32_t* sortbuf = reinterpret_cast<uint32_t*>(tk_smem);
-  uint32_t* hist = sortbuf + p.kpow2;
+  uint32_t* hist = sortbuf + NS;
   uint32_t* scan = hist + 256;
   uint32_t* warp_tot = scan + 256;
   uint32_t* misc = warp_tot + TK_WARPS + 4;
@@ -156,19 +154,19 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
       o.z = kv[4] | (kv[5] << 16);
       o.w = kv[6] | (kv[7] << 16);
       *reinterpret_cast<uint4*>(keys + i0) = o;
+      if (need_select) {
+#pragma unroll
+        for (int q = 0; q < TK_PER_THREAD; ++q) atomicAdd(hist + (kv[q] >> 8), 1u);
+      }
     } else {
 #pragma unroll
       for (int q = 0; q < TK_PER_THREAD; ++q) {
-        kv[q] = 0;
         if (i0 + q < L) {
           kv[q] = bf16_key(src[i0 + q]);
           keys[i0 + q] = (uint16_t)kv[q];
+          if (need_select) atomicAdd(hist + (kv[q] >> 8), 1u);
         }
       }
-    }
-    if (need_select) {
-#pragma unroll
-      for (int q = 0; q < TK_PER_THREAD; ++q) hist_add(hist, kv[q] >> 8, i0 + q < L);
     }
   }
   __syncthreads();
@@ -179,13 +177,24 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
     const uint32_t b1 = misc[0], above1 = misc[1];
     if (tid < 256) hist[tid] = 0;
     __syncthreads();
+    // low-byte histogram of the keys in bucket b1 only
     for (int base = 0; base < L; base += TK_CHUNK) {
       const int i0 = base + tid * TK_PER_THREAD;
+      if (i0 + TK_PER_THREAD <= L) {
+        const uint4 v = *reinterpret_cast<const uint4*>(keys + i0);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int q = 0; q < TK_PER_THREAD; ++q) {
-        const bool in = i0 + q < L;
-        const uint32_t key = in ? keys[i0 + q] : 0u;
-        hist_add(hist, key & 0xFFu, in && (key >> 8) == b1);
+        for (int q = 0; q < 4; ++q) {
+          if (((w[q] >> 8) & 0xFFu) == b1) atomicAdd(hist + (w[q] & 0xFFu), 1u);
+          if ((w[q] >> 24) == b1) atomicAdd(hist + ((w[q] >> 16) & 0xFFu), 1u);
+        }
+      } else {
+        for (int q = 0; q < TK_PER_THREAD; ++q) {
+          if (i0 + q < L) {
+            const uint32_t key = keys[i0 + q];
+            if ((key >> 8) == b1) atomicAdd(hist + (key & 0xFFu), 1u);
+          }
+        }
       }
     }
     __syncthreads();
@@ -195,86 +204,112 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
     need_eq = (uint32_t)K - above1 - above2;
   }
 
-  // ---- compaction in index order
+  // ---- compaction in index order: one scan of (equal << 16 | above) counts per chunk
   const int nsel = need_select ? K : L;
-  uint32_t eq_base = 0, sel_base = 0;
+  uint32_t gt_base = 0, eq_base = 0;
   for (int base = 0; base < L; base += TK_CHUNK) {
     const int i0 = base + tid * TK_PER_THREAD;
     uint32_t kq[TK_PER_THREAD];
-    uint32_t n_eq = 0;
+    if (i0 + TK_PER_THREAD <= L) {
+      const uint4 v = *reinterpret_cast<const uint4*>(keys + i0);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int q = 0; q < TK_PER_THREAD; ++q) {
-      kq[q] = (i0 + q < L) ? keys[i0 + q] : 0u;
-      n_eq += (i0 + q < L && kq[q] == thr) ? 1u : 0u;
+      for (int q = 0; q < 4; ++q) {
+        kq[2 * q] = w[q] & 0xFFFFu;
+        kq[2 * q + 1] = w[q] >> 16;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < TK_PER_THREAD; ++q) kq[q] = (i0 + q < L) ? keys[i0 + q] : 0u;
     }
-    uint32_t eq_tot;
-    const uint32_t eq_pre = need_select ? block_excl_scan(n_eq, warp_tot, eq_tot) : 0u;
-    uint32_t n_sel = 0;
-    uint32_t r = eq_base + eq_pre;
-    uint32_t selmask = 0;
+    uint32_t n_gt = 0, n_eq = 0;
 #pragma unroll
     for (int q = 0; q < TK_PER_THREAD; ++q) {
-      bool sel = false;
+      const bool in = i0 + q < L;
+      n_gt += (in && (!need_select || kq[q] > thr)) ? 1u : 0u;
+      n_eq += (in && need_select && kq[q] == thr) ? 1u : 0u;
+    }
+    uint32_t tot;
+    const uint32_t pre = block_excl_scan((n_eq << 16) | n_gt, warp_tot, tot);
+    uint32_t g = gt_base + (pre & 0xFFFFu), e = eq_base + (pre >> 16);
+#pragma unroll
+    for (int q = 0; q < TK_PER_THREAD; ++q) {
       if (i0 + q < L) {
+        int pos = -1;
         if (!need_select || kq[q] > thr) {
-          sel = true;
+          pos = (int)(g + (e < need_eq ? e : need_eq));
+          ++g;
         } else if (kq[q] == thr) {
-          sel = r < need_eq;
-          ++r;
+          if (e < need_eq) pos = (int)(g + e);
+          ++e;
         }
-      }
-      if (sel) {
-        selmask |= 1u << q;
-        ++n_sel;
+        if (pos >= 0 && pos < NS) sortbuf[pos] = ((0xFFFFu - kq[q]) << 16) | (uint32_t)(i0 + q);
       }
     }
-    uint32_t sel_tot;
-    uint32_t pos = sel_base + block_excl_scan(n_sel, warp_tot, sel_tot);
-#pragma unroll
-    for (int q = 0; q < TK_PER_THREAD; ++q) {
-      if (selmask & (1u << q)) {
-        if (pos < (uint32_t)p.kpow2)
-          sortbuf[pos] = ((0xFFFFu - kq[q]) << 16) | (uint32_t)(i0 + q);
-        ++pos;
-      }
-    }
-    if (need_select) eq_base += eq_tot;
-    sel_base += sel_tot;
+    gt_base += tot & 0xFFFFu;
+    eq_base += tot >> 16;
   }
-  // pad to the power of two
-  for (int i = nsel + tid; i < p.kpow2; i += TK_THREADS) sortbuf[i] = 0xFFFFFFFFu;
+  for (int i = nsel + tid; i < NS; i += TK_THREADS) sortbuf[i] = 0xFFFFFFFFu;
   __syncthreads();
 
-  // ---- bitonic sort, ascending composites
-  const int n = p.kpow2;
-  for (int kk = 2; kk <= n; kk <<= 1) {
+  // ---- bitonic sort of NS composites, ascending; thread t owns elements t*EPT ..
+  uint32_t v[EPT];
+#pragma unroll
+  for (int q = 0; q < EPT; ++q) v[q] = sortbuf[tid * EPT + q];
+#pragma unroll
+  for (int kk = 2; kk <= NS; kk <<= 1) {
+#pragma unroll
     for (int j = kk >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < n; i += TK_THREADS) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint32_t a = sortbuf[i], b = sortbuf[ixj];
-          const bool up = (i & kk) == 0;
-          if ((a > b) == up) {
-            sortbuf[i] = b;
-            sortbuf[ixj] = a;
+      if (j < EPT) {
+#pragma unroll
+        for (int q = 0; q < EPT; ++q) {
+          const int q2 = q ^ j;
+          if (q2 > q) {
+            const bool asc = ((tid * EPT + q) & kk) == 0;
+            const uint32_t lo = min(v[q], v[q2]), hi = max(v[q], v[q2]);
+            v[q] = asc ? lo : hi;
+            v[q2] = asc ? hi : lo;
           }
         }
+      } else if (j < 32 * EPT) {
+#pragma unroll
+        for (int q = 0; q < EPT; ++q) {
+          const uint32_t w = __shfl_xor_sync(0xFFFFFFFFu, v[q], j / EPT);
+          const int e = tid * EPT + q;
+          const bool take_min = ((e & j) == 0) == ((e & kk) == 0);
+          v[q] = take_min ? min(v[q], w) : max(v[q], w);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < EPT; ++q) sortbuf[tid * EPT + q] = v[q];
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < EPT; ++q) {
+          const int e = tid * EPT + q;
+          const uint32_t w = sortbuf[e ^ j];
+          const bool take_min = ((e & j) == 0) == ((e & kk) == 0);
+          v[q] = take_min ? min(v[q], w) : max(v[q], w);
+        }
+        __syncthreads();
       }
-      __syncthreads();
     }
   }
 
   // ---- post-process and write
-  for (int i = tid; i < K; i += TK_THREADS) {
-    int64_t o = -1;
-    if (i < nsel) {
-      const int64_t idx = (int64_t)(sortbuf[i] & 0xFFFFu);
-      o = (p.causal && idx >= lim64) ? -1 : idx + p.offset;
+#pragma unroll
+  for (int q = 0; q < EPT; ++q) {
+    const int i = tid * EPT + q;
+    if (i < K) {
+      int64_t o = -1;
+      if (i < nsel) {
+        const int64_t idx = (int64_t)(v[q] & 0xFFFFu);
+        o = (p.causal && idx >= lim64) ? -1 : idx + p.offset;
+      }
+      if (p.out_i64)
+        reinterpret_cast<int64_t*>(p.out)[row * p.out_row_stride + i] = o;
+      else
+        reinterpret_cast<int32_t*>(p.out)[row * p.out_row_stride + i] = (int32_t)o;
     }
-    if (p.out_i64)
-      reinterpret_cast<int64_t*>(p.out)[row * p.out_row_stride + i] = o;
-    else
-      reinterpret_cast<int32_t*>(p.out)[row * p.out_row_stride + i] = (int32_t)o;
   }
 }
 
