@@ -38,6 +38,7 @@ struct IndexerScoreParams {
   const float* freqs;  // [S, rd/2, 2] (cos, sin) for the rows' positions
   const uint16_t* w;   // bf16 [B, S, H] (batch stride w_bs elements)
   int64_t w_bs;
+  int32_t w_vec16;     // w and w_bs allow 16-byte loads
   uint16_t* scores;    // bf16 [B*S, score_ld]
   int64_t score_ld;
   int32_t B, S, H, D, T, rd;
@@ -167,8 +168,8 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
         const uint32_t qaddr = smem_u32(qbuf + qs * q_bytes);
         for (int t = 0; t < nt; ++t) {
           const int st = kc % p.kst, as = ac & 1;
-          if (!(ok = mbar_wait(&sh->acc_empty[as], ((ac >> 1) & 1) ^ 1, wc))) break;
-          if (!(ok = mbar_wait(&sh->k_full[st], (kc / p.kst) & 1, wc))) break;
+          if (!(ok = mbar_wait_inl(&sh->acc_empty[as], ((ac >> 1) & 1) ^ 1, wc))) break;
+          if (!(ok = mbar_wait_inl(&sh->k_full[st], (kc / p.kst) & 1, wc))) break;
           tc_fence_after();
           const uint32_t kaddr = smem_u32(kbuf + st * k_bytes);
           const uint32_t d_tmem = tmem + as * IX_N;
@@ -233,6 +234,8 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Thread = key (TMEM lane); two tokens at a time, their head sums carried
+    // as one f32x2 pair (each token still summed in head order, round to nearest).
     const int e = warp - IX_EPI_WARP0;  // 0..7
     const int quarter = warp & 3;       // TMEM lanes [32*quarter, +32) belong to this warp
     const int half = e >> 2;            // which half of the item's tokens
@@ -246,38 +249,67 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
       bool ok = true;
       for (int t = 0; t < nt; ++t) {
         const int as = ac & 1;
-        if (!(ok = mbar_wait(&sh->acc_full[as], (ac >> 1) & 1, wc))) break;
+        if (!(ok = mbar_wait_inl(&sh->acc_full[as], (ac >> 1) & 1, wc))) break;
         tc_fence_after();
         const int key = t * IX_TILE_KEYS + quarter * 32 + lane;
 #pragma unroll 1
-        for (int jj = 0; jj < TOK_HALF; ++jj) {
-          const int j = half * TOK_HALF + jj;
-          const int s = g * TOK + j;
-          // head weights of token s as bf16 pairs (warp-uniform loads, L1 resident)
-          const uint32_t* w2 = reinterpret_cast<const uint32_t*>(
-              p.w + (int64_t)b * p.w_bs + (int64_t)(s < p.S ? s : p.S - 1) * H);
-          const uint32_t col = tmem + as * IX_N + j * H + ((uint32_t)(quarter * 32) << 16);
-          uint32_t r[H];
+        for (int jp = 0; jp < TOK_HALF; jp += 2) {
+          const int j0 = half * TOK_HALF + jp;
+          const int s0 = g * TOK + j0, s1 = s0 + 1;
+          // head weights of the two tokens (warp-uniform loads, L1 resident)
+          const uint16_t* wrow0 = p.w + (int64_t)b * p.w_bs + (int64_t)(s0 < p.S ? s0 : p.S - 1) * H;
+          const uint16_t* wrow1 = p.w + (int64_t)b * p.w_bs + (int64_t)(s1 < p.S ? s1 : p.S - 1) * H;
+          const uint32_t col0 = tmem + as * IX_N + j0 * H + ((uint32_t)(quarter * 32) << 16);
+          uint64_t acc = 0;  // (token s0, token s1) partial sums, f32x2
 #pragma unroll
-          for (int c = 0; c < H; c += 16) tmem_ld16(col + c, r + c);
-          tmem_wait_ld();
-          float acc = 0.f;
+          for (int c = 0; c < H; c += 16) {
+            uint32_t r0[16], r1[16];
+            tmem_ld16(col0 + c, r0);
+            tmem_ld16(col0 + H + c, r1);
+            uint32_t w0[8], w1[8];
+            if (p.w_vec16) {
+              const uint4 a0 = __ldg(reinterpret_cast<const uint4*>(wrow0 + c));
+              const uint4 a1 = __ldg(reinterpret_cast<const uint4*>(wrow0 + c + 8));
+              const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(wrow1 + c));
+              const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(wrow1 + c + 8));
+              w0[0] = a0.x; w0[1] = a0.y; w0[2] = a0.z; w0[3] = a0.w;
+              w0[4] = a1.x; w0[5] = a1.y; w0[6] = a1.z; w0[7] = a1.w;
+              w1[0] = b0.x; w1[1] = b0.y; w1[2] = b0.z; w1[3] = b0.w;
+              w1[4] = b1.x; w1[5] = b1.y; w1[6] = b1.z; w1[7] = b1.w;
+            } else {
 #pragma unroll
-          for (int h = 0; h < H; h += 2) {
-            uint32_t pr = cvt_relu_bf16x2(__uint_as_float(r[h]), __uint_as_float(r[h + 1]));
-            pr = mul_bf16x2(pr, __ldg(w2 + (h >> 1)));
-            acc = __fadd_rn(acc, bf16lo_f32(pr));
-            acc = __fadd_rn(acc, bf16hi_f32(pr));
+              for (int i = 0; i < 8; ++i) {
+                w0[i] = __ldg(reinterpret_cast<const uint32_t*>(wrow0 + c) + i);
+                w1[i] = __ldg(reinterpret_cast<const uint32_t*>(wrow1 + c) + i);
+              }
+            }
+            tmem_wait_ld();
+#pragma unroll
+            for (int h = 0; h < 16; h += 2) {
+              const uint32_t p0 = mul_bf16x2(cvt_relu_bf16x2(__uint_as_float(r0[h]), __uint_as_float(r0[h + 1])), w0[h >> 1]);
+              const uint32_t p1 = mul_bf16x2(cvt_relu_bf16x2(__uint_as_float(r1[h]), __uint_as_float(r1[h + 1])), w1[h >> 1]);
+              // head h (low halves), then head h + 1 (high halves)
+              asm("{ .reg .b64 t; mov.b64 t, {%1, %2}; add.rn.f32x2 %0, %0, t; }"
+                  : "+l"(acc) : "r"(p0 << 16), "r"(p1 << 16));
+              asm("{ .reg .b64 t; mov.b64 t, {%1, %2}; add.rn.f32x2 %0, %0, t; }"
+                  : "+l"(acc) : "r"(p0 & 0xFFFF0000u), "r"(p1 & 0xFFFF0000u));
+            }
           }
-          int64_t lim = p.T;
-          if (p.causal) {
-            const int64_t l2 = (p.pos0 + s + 1) / p.ratio;
-            lim = l2 < lim ? l2 : lim;
+          float acc0, acc1;
+          asm("mov.b64 {%0, %1}, %2;" : "=f"(acc0), "=f"(acc1) : "l"(acc));
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int s = u ? s1 : s0;
+            int64_t lim = p.T;
+            if (p.causal) {
+              const int64_t l2 = (p.pos0 + s + 1) / p.ratio;
+              lim = l2 < lim ? l2 : lim;
+            }
+            uint16_t out = __bfloat16_as_ushort(__float2bfloat16_rn(u ? acc1 : acc0));
+            if (key >= lim) out = 0xFF80;  // -inf
+            if (s < p.S && key < p.T)
+              p.scores[((int64_t)b * p.S + s) * p.score_ld + key] = out;
           }
-          uint16_t out = __bfloat16_as_ushort(__float2bfloat16_rn(acc));
-          if (key >= lim) out = 0xFF80;  // -inf
-          if (s < p.S && key < p.T)
-            p.scores[((int64_t)b * p.S + s) * p.score_ld + key] = out;
         }
         tc_fence_before();
         __syncwarp();

@@ -189,6 +189,7 @@ int indexer_scores_impl(const void* q, const void* k, int64_t k_batch_rows, cons
   p.freqs = freqs;
   p.w = static_cast<const uint16_t*>(w);
   p.w_bs = S * H;
+  p.w_vec16 = aligned(w, 16) ? 1 : 0;  // rows of H >= 16 bf16 are 16-byte multiples
   p.scores = static_cast<uint16_t*>(scores);
   p.score_ld = score_ld;
   p.B = (int)B; p.S = (int)S; p.H = (int)H; p.D = (int)D; p.T = (int)T; p.rd = rope_dim;
