@@ -29,10 +29,10 @@
 // into registers and 16-byte shared stores (the swizzle computed per store) into
 // the 128-byte-swizzled layouts the MMAs read (K-major for QK, MN-major for PV).
 // A thread's proxy fence and barrier arrive wait for every load it still has in
-// flight, so one thread cannot overlap two chunks; instead four groups of two
-// warps take turns (group g fills chunks g, g + 4, ...): each group loads a whole
+// flight, so one thread cannot overlap two chunks; instead five groups of two
+// warps take turns (group g fills chunks g, g + 5, ...): each group loads a whole
 // chunk into registers (16 loads per thread) before its slot is free, so up to
-// 64 KB per SM are in flight while the slots turn over.  Measured per SM on
+// 80 KB per SM are in flight while the slots turn over.  Measured per SM on
 // random rows: register-staged loads reach ~120 GB/s with 32 KB in flight;
 // cp.async saturates near 16 KB in flight (~55 GB/s) and TMA tile::gather4 near
 // 48 GB/s with 16 issuing warps.  Per 256 keys an SM runs 36 + 32 MMAs of 64
@@ -40,10 +40,10 @@
 //
 // Roles per CTA (16 warps; registers are granted per four warps, so 13 would
 // cost the same):
-//   warps 0-7   four gather groups,
+//   warps 0-7   four gather groups (warps 2g, 2g + 1),
 //   warps 8, 9  issue the MMAs in CTA 0: warp 8 the QK chunks, warp 9 the V
 //               chunks; in CTA 1 warp 8 forwards "query tile landed",
-//   warps 10-11 idle,
+//   warps 10-11 a fifth gather group,
 //   warps 12-15 online softmax (base 2, lazy rescaling of O when the running max
 //               grows by more than 2^8) and the epilogue.
 // TMEM lane l holds head (l mod 64); lanes l and l+64 hold the two halves of that
@@ -61,9 +61,8 @@ namespace ks {
 #endif
 
 constexpr int SA_THREADS = 512;
-constexpr int SA_GROUPS = 4;        // gather groups
+constexpr int SA_GROUPS = 5;        // gather groups (warps 0-7 and 10-11)
 constexpr int SA_GROUP = 64;        // threads per gather group
-constexpr int SA_PROD_WARPS = SA_GROUPS * SA_GROUP / 32;
 constexpr int SA_MMA_WARP = 8;
 constexpr int SA_SMX_WARP0 = 12;
 constexpr int SA_SMX_WARPS = 4;
@@ -205,7 +204,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
     }
   };
 
-  if (warp < SA_PROD_WARPS) {
+  if (warp < 8 || warp == 10 || warp == 11) {
     // ------------------------------------------------------------ gathers
     // Group g (warps 2g, 2g + 1) fills ring positions g, g + 4, ...  Thread u of
     // the group moves 16-byte piece c = u % 8 of keys rg + 8 i, rg = u / 8:
@@ -215,7 +214,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
     // atom.  The raw indices of the group's next chunk are fetched with the
     // current chunk's loads; the round's fence has waited for them by the time
     // they are used.
-    const int g = warp >> 1;
+    const int g = warp < 8 ? warp >> 1 : 4;
     const int u = ((warp & 1) << 5) | lane;
     const int c = u & 7, rg = u >> 3;
     const uint32_t swz = (uint32_t)((c ^ rg) << 4);
