@@ -11,8 +11,8 @@
  *
  * Kernels never spin without bound: a wait that runs out of its time budget
  * (KS_WAIT_BUDGET_MS in the environment, default 2000 ms) records an error in a
- * per-device status word and the kernel returns.  ks_device_status() reads and
- * clears that word.
+ * per-device status record (the code and where the first timeout happened) and
+ * the kernel returns.  ks_device_status() reads and clears that record.
  */
 #ifndef KS_B200_H
 #define KS_B200_H
@@ -143,16 +143,18 @@ int ks_indexer_noalloc(const void* q, const void* k, int64_t k_batch_rows, const
                        int32_t topk, int64_t offset, void* out, int32_t out_dtype, void* stream);
 
 /*
- * Synchronise `stream`, then read and clear the current device's status word:
+ * Synchronise `stream`, then read and clear the current device's status record:
  * KS_OK, or KS_ERR_DEVICE when a kernel reported a timed-out wait or a bounds
- * error since the last call.  No counterpart in the reference.
+ * error since the last call (ks_last_error() then names the block, thread,
+ * barrier and progress tag of the first timed-out wait).  No counterpart in the
+ * reference.
  */
 int ks_device_status(void* stream);
 
 /*
  * Self-test of the bounded-wait path: launches one CTA that waits on a barrier
  * nobody completes, with the given budget; the wait gives up, records a
- * timeout in the status word and the kernel returns.  No counterpart in the
+ * timeout in the status record and the kernel returns.  No counterpart in the
  * reference.
  */
 int ks_selftest_wait_timeout(uint64_t budget_ns, void* stream);
