@@ -20,8 +20,32 @@ namespace ks {
 
 constexpr int SK_THREADS = 128;
 
-// 1/d, correctly rounded (used once per row or column per normalisation).
-__device__ __forceinline__ float sk_rcp(float d) { return __frcp_rn(d); }
+// 1/d from the hardware reciprocal (rcp.approx: within 1 ulp; d >= eps > 0 here).
+__device__ __forceinline__ float sk_rcp(float d) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  return r;
+}
+// Two fp32 lanes in one 64-bit register: add/mul.rn.f32x2 do two IEEE operations
+// per instruction.
+__device__ __forceinline__ uint64_t sk_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void sk_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t sk_add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t sk_mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 
 template <int N>
 __global__ void __launch_bounds__(SK_THREADS)
@@ -63,45 +87,92 @@ __global__ void __launch_bounds__(SK_THREADS)
 #pragma unroll
       for (int j = 0; j < N; ++j) a[i][j] = my[i * N + j];
 
-    // softmax over the last dim, then + eps
+    // softmax over the last dim, then + eps (exp through ex2 of x * log2(e))
+    constexpr float kLog2e = 1.4426950408889634f;
 #pragma unroll
     for (int i = 0; i < N; ++i) {
       float m = a[i][0];
 #pragma unroll
       for (int j = 1; j < N; ++j) m = fmaxf(m, a[i][j]);
+      const float mb = m * kLog2e;
       float s = 0.f;
 #pragma unroll
       for (int j = 0; j < N; ++j) {
-        a[i][j] = expf(a[i][j] - m);
+        a[i][j] = exp2f(fmaf(a[i][j], kLog2e, -mb));
         s += a[i][j];
       }
       const float r = sk_rcp(s);
 #pragma unroll
-      for (int j = 0; j < N; ++j) a[i][j] = a[i][j] * r + eps;
+      for (int j = 0; j < N; ++j) a[i][j] = fmaf(a[i][j], r, eps);
     }
-    // baseline/sinkhorn.py:15-18: one column pass, then repeat-1 (row, column) pairs
     const int rounds = repeat < 1 ? 1 : repeat;
-    for (int it = 0; it < rounds; ++it) {
-      if (it > 0) {  // row normalisation (skipped in the first round)
+    if constexpr (N % 2 == 0) {
+      // pairs of adjacent columns: p[i][c] = (a[i][2c], a[i][2c + 1])
+      constexpr int C = N / 2;
+      uint64_t pr[N][C];
 #pragma unroll
-        for (int i = 0; i < N; ++i) {
-          float s = 0.f;
+      for (int i = 0; i < N; ++i)
 #pragma unroll
-          for (int j = 0; j < N; ++j) s += a[i][j];
-          const float r = sk_rcp(s + eps);
+        for (int c = 0; c < C; ++c) pr[i][c] = sk_pack(a[i][2 * c], a[i][2 * c + 1]);
+      const uint64_t eps2 = sk_pack(eps, eps);
+      // baseline/sinkhorn.py:15-18: one column pass, then repeat-1 (row, column) pairs
+      for (int it = 0; it < rounds; ++it) {
+        if (it > 0) {  // row normalisation (skipped in the first round)
 #pragma unroll
-          for (int j = 0; j < N; ++j) a[i][j] *= r;
+          for (int i = 0; i < N; ++i) {
+            uint64_t sp = pr[i][0];
+#pragma unroll
+            for (int c = 1; c < C; ++c) sp = sk_add2(sp, pr[i][c]);
+            float lo, hi;
+            sk_unpack(sp, lo, hi);
+            const float r = sk_rcp(lo + hi + eps);
+            const uint64_t r2 = sk_pack(r, r);
+#pragma unroll
+            for (int c = 0; c < C; ++c) pr[i][c] = sk_mul2(pr[i][c], r2);
+          }
+        }
+        // column normalisation, two columns at a time
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+          uint64_t sp = pr[0][c];
+#pragma unroll
+          for (int i = 1; i < N; ++i) sp = sk_add2(sp, pr[i][c]);
+          sp = sk_add2(sp, eps2);
+          float lo, hi;
+          sk_unpack(sp, lo, hi);
+          const uint64_t r2 = sk_pack(sk_rcp(lo), sk_rcp(hi));
+#pragma unroll
+          for (int i = 0; i < N; ++i) pr[i][c] = sk_mul2(pr[i][c], r2);
         }
       }
-      // column normalisation
 #pragma unroll
-      for (int j = 0; j < N; ++j) {
-        float s = 0.f;
+      for (int i = 0; i < N; ++i)
 #pragma unroll
-        for (int i = 0; i < N; ++i) s += a[i][j];
-        const float r = sk_rcp(s + eps);
+        for (int c = 0; c < C; ++c) sk_unpack(pr[i][c], a[i][2 * c], a[i][2 * c + 1]);
+    } else {
+      // baseline/sinkhorn.py:15-18: one column pass, then repeat-1 (row, column) pairs
+      for (int it = 0; it < rounds; ++it) {
+        if (it > 0) {  // row normalisation (skipped in the first round)
 #pragma unroll
-        for (int i = 0; i < N; ++i) a[i][j] *= r;
+          for (int i = 0; i < N; ++i) {
+            float s = 0.f;
+#pragma unroll
+            for (int j = 0; j < N; ++j) s += a[i][j];
+            const float r = sk_rcp(s + eps);
+#pragma unroll
+            for (int j = 0; j < N; ++j) a[i][j] *= r;
+          }
+        }
+        // column normalisation
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          float s = 0.f;
+#pragma unroll
+          for (int i = 0; i < N; ++i) s += a[i][j];
+          const float r = sk_rcp(s + eps);
+#pragma unroll
+          for (int i = 0; i < N; ++i) a[i][j] *= r;
+        }
       }
     }
     float* myw = sk_smem + tid * STRIDE;
