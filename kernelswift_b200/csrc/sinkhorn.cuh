@@ -12,6 +12,7 @@
 // 128 threads stages its 128 contiguous matrices through shared memory so the
 // HBM traffic is 128-bit coalesced; the per-thread copy uses an odd word stride
 // (n*n + 1) so shared-memory reads are free of bank conflicts.
+// Scaling path (even n <= 8, used for those sizes): see sinkhorn_scale_kernel.
 // Warp path (8 < n <= 64): one warp per matrix in shared memory.
 #pragma once
 #include "ks_device.cuh"
@@ -44,6 +45,11 @@ __device__ __forceinline__ uint64_t sk_add2(uint64_t a, uint64_t b) {
 __device__ __forceinline__ uint64_t sk_mul2(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t sk_fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
   return r;
 }
 
@@ -196,6 +202,144 @@ __global__ void __launch_bounds__(SK_THREADS)
       int m = e / NN, o = e % NN;
       __stcs(dst + e, sk_smem[m * STRIDE + o]);
     }
+  }
+}
+
+// Scaling path (even n <= 8): one thread per matrix; the iteration is carried as
+//   x_ij = u_i K_ij v_j,  K = softmax(x) + eps,  u = v = 1,
+// which is the reference's sequence of normalisations written with row and column
+// scale vectors:
+//   column pass:  v_j <- v_j / (v_j (u^T K)_j + eps)
+//   row pass:     u_i <- u_i / (u_i (K v)_i + eps)
+// so each pass is one matrix-vector product (n^2 FMAs, two columns at a time as
+// f32x2) plus n reciprocals, instead of rewriting all n^2 entries (sums and
+// products) every pass.  The result x_ij = u_i K_ij v_j is formed once at the end.
+// Only the rounding differs from the reference's entry-wise updates.
+template <int N>
+__global__ void __launch_bounds__(SK_THREADS)
+    sinkhorn_scale_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t n_mats,
+                          int repeat, float eps) {
+  static_assert(N % 2 == 0 && N <= 8, "scaling path: even n <= 8");
+  constexpr int NN = N * N;
+  constexpr int C = N / 2;
+  constexpr int STRIDE = NN + 1;  // odd word stride: conflict-free per-thread access
+  extern __shared__ float sk_smem[];
+  const int tid = threadIdx.x;
+  const int64_t mat0 = (int64_t)blockIdx.x * SK_THREADS;
+  const int nm = (int)min((int64_t)SK_THREADS, n_mats - mat0);
+  const float* src = x + mat0 * NN;
+  float* dst = out + mat0 * NN;
+  const int total = nm * NN;
+
+  // coalesced load of the block's contiguous chunk into the padded layout
+  if (nm == SK_THREADS && (NN % 4) == 0) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    for (int v = tid; v < total / 4; v += SK_THREADS) {
+      float4 f = __ldcs(s4 + v);
+      int e = v * 4;
+      float* d = sk_smem + (e / NN) * STRIDE + e % NN;
+      d[0] = f.x; d[1] = f.y; d[2] = f.z; d[3] = f.w;
+    }
+  } else {
+    for (int e = tid; e < total; e += SK_THREADS) sk_smem[(e / NN) * STRIDE + e % NN] = __ldcs(src + e);
+  }
+  __syncthreads();
+
+  if (tid < nm) {
+    const float* my = sk_smem + tid * STRIDE;
+    // K = softmax(x) + eps, kept as column pairs kp[i][c] = (K[i][2c], K[i][2c+1])
+    uint64_t kp[N][C];
+    constexpr float kLog2e = 1.4426950408889634f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      float r[N];
+#pragma unroll
+      for (int j = 0; j < N; ++j) r[j] = my[i * N + j];
+      float m = r[0];
+#pragma unroll
+      for (int j = 1; j < N; ++j) m = fmaxf(m, r[j]);
+      const float mb = m * kLog2e;
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        r[j] = exp2f(fmaf(r[j], kLog2e, -mb));
+        s += r[j];
+      }
+      const float rs = sk_rcp(s);
+#pragma unroll
+      for (int c = 0; c < C; ++c) kp[i][c] = sk_pack(fmaf(r[2 * c], rs, eps), fmaf(r[2 * c + 1], rs, eps));
+    }
+    float u[N], v[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) u[i] = 1.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = 1.f;
+    const int rounds = repeat < 1 ? 1 : repeat;
+    // baseline/sinkhorn.py:15-18: one column pass, then repeat-1 (row, column) pairs
+    for (int it = 0; it < rounds; ++it) {
+      if (it > 0) {  // row pass: u_i <- u_i / (u_i (K v)_i + eps)
+        uint64_t vp[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) vp[c] = sk_pack(v[2 * c], v[2 * c + 1]);
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          uint64_t acc = sk_mul2(kp[i][0], vp[0]);
+#pragma unroll
+          for (int c = 1; c < C; ++c) acc = sk_fma2(kp[i][c], vp[c], acc);
+          float lo, hi;
+          sk_unpack(acc, lo, hi);
+          u[i] = u[i] * sk_rcp(fmaf(u[i], lo + hi, eps));
+        }
+      }
+      // column pass: v_j <- v_j / (v_j (u^T K)_j + eps), two columns at a time
+      uint64_t t[C];
+      {
+        const uint64_t u0 = sk_pack(u[0], u[0]);
+#pragma unroll
+        for (int c = 0; c < C; ++c) t[c] = sk_mul2(kp[0][c], u0);
+      }
+#pragma unroll
+      for (int i = 1; i < N; ++i) {
+        const uint64_t ui = sk_pack(u[i], u[i]);
+#pragma unroll
+        for (int c = 0; c < C; ++c) t[c] = sk_fma2(kp[i][c], ui, t[c]);
+      }
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        float lo, hi;
+        sk_unpack(t[c], lo, hi);
+        v[2 * c] = v[2 * c] * sk_rcp(fmaf(v[2 * c], lo, eps));
+        v[2 * c + 1] = v[2 * c + 1] * sk_rcp(fmaf(v[2 * c + 1], hi, eps));
+      }
+    }
+    // x_ij = u_i K_ij v_j
+    uint64_t vp[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) vp[c] = sk_pack(v[2 * c], v[2 * c + 1]);
+    float* myw = sk_smem + tid * STRIDE;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const uint64_t ui = sk_pack(u[i], u[i]);
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        float lo, hi;
+        sk_unpack(sk_mul2(sk_mul2(kp[i][c], ui), vp[c]), lo, hi);
+        myw[i * N + 2 * c] = lo;
+        myw[i * N + 2 * c + 1] = hi;
+      }
+    }
+  }
+  __syncthreads();
+
+  if (nm == SK_THREADS && (NN % 4) == 0) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    for (int v = tid; v < total / 4; v += SK_THREADS) {
+      int e = v * 4;
+      const float* s = sk_smem + (e / NN) * STRIDE + e % NN;
+      __stcs(d4 + v, make_float4(s[0], s[1], s[2], s[3]));
+    }
+  } else {
+    for (int e = tid; e < total; e += SK_THREADS) __stcs(dst + e, sk_smem[(e / NN) * STRIDE + e % NN]);
   }
 }
 
