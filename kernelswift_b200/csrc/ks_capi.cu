@@ -311,6 +311,12 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
   const size_t avail = limit > p.r_off ? limit - p.r_off : 0;
   int ns = (int)(avail / SA_SLOT);
   if (ns > SA_MAX_SLOTS) ns = SA_MAX_SLOTS;
+  // A multiple of the gather groups, so every use of a slot falls to the same
+  // group (position n: slot n mod ns, group n mod SA_GROUPS).  The "slot empty"
+  // waits are parity waits, which only hold when the waiter is at most one phase
+  // ahead of the barrier; a group that did not fill the slot's previous round
+  // could be two ahead of it and would overwrite a chunk not yet consumed.
+  ns -= ns % SA_GROUPS;
   if (ns < SA_GROUPS)
     return fail(KS_ERR_UNSUPPORTED, "sparse_attn: shared memory too small for D=%lld", (long long)D);
   p.n_slots = ns;

@@ -70,7 +70,7 @@ constexpr int SA_NB = 256;          // keys per block
 constexpr int SA_HALF = 128;        // keys per CTA in the QK product
 constexpr int SA_KC = 32;           // keys per V chunk
 constexpr int SA_NKC = SA_NB / SA_KC;
-constexpr int SA_MAX_SLOTS = 12;    // ring slots
+constexpr int SA_MAX_SLOTS = 10;    // ring slots (a multiple of SA_GROUPS)
 constexpr int SA_HDR = 2048;        // shared header bytes
 constexpr uint32_t SA_SLOT = SA_HALF * 128;    // 16 KB: 128 keys x 64 dims bf16
 constexpr uint32_t SA_VSEG = SA_KC * 128;      // one 64-column V segment of a chunk
@@ -206,7 +206,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
 
   if (warp < 8 || warp == 10 || warp == 11) {
     // ------------------------------------------------------------ gathers
-    // Group g (warps 2g, 2g + 1) fills ring positions g, g + 4, ...  Thread u of
+    // Group g (warps 2g, 2g + 1) fills ring positions g, g + 5, ...  Thread u of
     // the group moves 16-byte piece c = u % 8 of keys rg + 8 i, rg = u / 8:
     //   QK chunk: i < 16 (the CTA's 128 keys of the block), dims 64 sub + 8 c;
     //   V chunk:  i < 4 (keys 32 sub + ..), each of the CTA's n_pvblk V segments.
@@ -266,6 +266,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         }
       }
       fetch(n + SA_GROUPS);
+      // n_slots is a multiple of SA_GROUPS, so this group alone fills this slot
+      // and its parity wait is never two phases ahead of the barrier.
       const int slot = (int)(n % (uint32_t)p.n_slots);
       wc.tag = (int)n;
       if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->empty[slot], ((n / p.n_slots) & 1) ^ 1, wc))))

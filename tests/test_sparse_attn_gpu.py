@@ -128,3 +128,25 @@ def test_mla_scale_rows(cuda_ok):
         ib = idx[b:b + 1, rows].cpu().numpy()
         ref = O.sparse_attn(qb, bits_from_bf16(kv[b:b + 1]), sink.cpu().numpy(), ib, D ** -0.5, dv)
         assert_close(bits_from_bf16(out[b:b + 1, rows]), ref)
+
+
+@pytest.mark.parametrize("B,M,H,D,N,K,dv,mode", [
+    CASES[0],                                   # D = 128: room for 9 ring slots, 5 used
+    CASES[4],                                   # D = 192: room for 8
+    (2, 16, 128, 192, 4096, 1024, 192, "perm"),  # four key blocks per query
+])
+def test_repeatable(cuda_ok, B, M, H, D, N, K, dv, mode):
+    """Repeated calls give bit-identical results.  Guards the ring sizing: with a
+    slot count that is not a multiple of the gather groups, a group could pass its
+    "slot empty" parity wait two phases early and overwrite a chunk in use, which
+    shows up as run-to-run differences."""
+    from kernelswift_b200 import ops
+
+    q, kv, s, idx = make_case(B, M, H, D, N, K, seed=7 + D + K, mode=mode)
+    q, kv, s, idx = q.cuda(), kv.cuda(), s.cuda(), idx.cuda()
+    outs = [ops.sparse_attn(q, kv, s, idx, D ** -0.5, dv) for _ in range(4)]
+    ops.device_status()
+    for o in outs[1:]:
+        assert torch.equal(outs[0], o)
+    ref = O.sparse_attn(bits_from_bf16(q), bits_from_bf16(kv), s.cpu().numpy(), idx.cpu().numpy(), D ** -0.5, dv)
+    assert_close(bits_from_bf16(outs[0]), ref)
