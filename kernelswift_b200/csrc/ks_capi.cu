@@ -408,17 +408,23 @@ int ks_sinkhorn(const float* x, float* out, int64_t n_mats, int32_t n, int32_t r
     const size_t smem = (size_t)SK_THREADS * (N * N + 1) * 4;
     kern<<<(unsigned)blocks_reg, SK_THREADS, smem, st>>>(x, out, n_mats, repeat, eps);
   };
-  if (blocks_reg > 0x7FFFFFFFll) return fail(KS_ERR_UNSUPPORTED, "sinkhorn: too many matrices");
+  if (blocks_reg > 0x7FFFFFFFll / 2) return fail(KS_ERR_UNSUPPORTED, "sinkhorn: too many matrices");
+  // even n <= 8: two threads per matrix (SK_THREADS / 2 matrices per block)
+  auto launch_pair = [&](auto kern, int N) {
+    const int64_t blocks = (n_mats + SK_THREADS / 2 - 1) / (SK_THREADS / 2);
+    const size_t smem = (size_t)(SK_THREADS / 2) * (N * N + 2) * 4;
+    kern<<<(unsigned)blocks, SK_THREADS, smem, st>>>(x, out, n_mats, repeat, eps);
+  };
 
   switch (n) {
     case 1: launch_reg(sinkhorn_reg_kernel<1>, 1); break;
-    case 2: launch_reg(sinkhorn_scale_kernel<2>, 2); break;
+    case 2: launch_pair(sinkhorn_pair_kernel<2>, 2); break;
     case 3: launch_reg(sinkhorn_reg_kernel<3>, 3); break;
-    case 4: launch_reg(sinkhorn_scale_kernel<4>, 4); break;
+    case 4: launch_pair(sinkhorn_pair_kernel<4>, 4); break;
     case 5: launch_reg(sinkhorn_reg_kernel<5>, 5); break;
-    case 6: launch_reg(sinkhorn_scale_kernel<6>, 6); break;
+    case 6: launch_pair(sinkhorn_pair_kernel<6>, 6); break;
     case 7: launch_reg(sinkhorn_reg_kernel<7>, 7); break;
-    case 8: launch_reg(sinkhorn_scale_kernel<8>, 8); break;
+    case 8: launch_pair(sinkhorn_pair_kernel<8>, 8); break;
     default: {
       static std::once_flag once;
       std::call_once(once, [] {

@@ -12,7 +12,7 @@
 // 128 threads stages its 128 contiguous matrices through shared memory so the
 // HBM traffic is 128-bit coalesced; the per-thread copy uses an odd word stride
 // (n*n + 1) so shared-memory reads are free of bank conflicts.
-// Scaling path (even n <= 8, used for those sizes): see sinkhorn_scale_kernel.
+// Scaling path (even n <= 8): see sinkhorn_pair_kernel (two threads per matrix).
 // Warp path (8 < n <= 64): one warp per matrix in shared memory.
 #pragma once
 #include "ks_device.cuh"
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(SK_THREADS)
   }
 }
 
-// Scaling path (even n <= 8): one thread per matrix; the iteration is carried as
+// Scaling path (even n <= 8).  The iteration is carried as
 //   x_ij = u_i K_ij v_j,  K = softmax(x) + eps,  u = v = 1,
 // which is the reference's sequence of normalisations written with row and column
 // scale vectors:
@@ -215,46 +215,67 @@ __global__ void __launch_bounds__(SK_THREADS)
 // f32x2) plus n reciprocals, instead of rewriting all n^2 entries (sums and
 // products) every pass.  The result x_ij = u_i K_ij v_j is formed once at the end.
 // Only the rounding differs from the reference's entry-wise updates.
+// Two threads per matrix, so twice as many warps hide the latency of the
+// per-matrix chain (one thread per matrix leaves a C5-sized batch at ~14 warps
+// per SM).  Thread h of a pair (lanes 2k, 2k + 1) owns rows [h n/2, (h+1) n/2) of
+// K and their u, and keeps all of v.  Each thread holds its columns rotated by
+// h n/2, so local columns 0 .. n/2-1 are the ones whose v it updates and local
+// column n/2 + k of one thread is local column k of its partner.  Row pass:
+// local.  Column pass: each thread forms the partial column sums of its rows;
+// one shuffle per column brings the partner's part of the columns this thread
+// updates, and one more returns the new v.  The reciprocal count per matrix is
+// that of the one-thread form.
+// Shared staging: a matrix's two row halves sit at word offsets 0 and n^2/2 + 1
+// (matrix stride n^2 + 2), which keeps a warp's per-thread reads on 32 distinct
+// banks.
 template <int N>
 __global__ void __launch_bounds__(SK_THREADS)
-    sinkhorn_scale_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t n_mats,
-                          int repeat, float eps) {
-  static_assert(N % 2 == 0 && N <= 8, "scaling path: even n <= 8");
+    sinkhorn_pair_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t n_mats,
+                         int repeat, float eps) {
+  static_assert(N % 2 == 0 && N <= 8, "pair path: even n <= 8");
   constexpr int NN = N * N;
-  constexpr int C = N / 2;
-  constexpr int STRIDE = NN + 1;  // odd word stride: conflict-free per-thread access
+  constexpr int R = N / 2;         // rows per thread, and columns whose v it updates
+  constexpr int C = N / 2;         // column pairs
+  constexpr int HW = NN / 2;       // words per row half
+  constexpr int STRIDE = NN + 2;
+  constexpr int MPB = SK_THREADS / 2;
   extern __shared__ float sk_smem[];
   const int tid = threadIdx.x;
-  const int64_t mat0 = (int64_t)blockIdx.x * SK_THREADS;
-  const int nm = (int)min((int64_t)SK_THREADS, n_mats - mat0);
+  const int ml = tid >> 1, h = tid & 1;
+  const int64_t mat0 = (int64_t)blockIdx.x * MPB;
+  const int nm = (int)min((int64_t)MPB, n_mats - mat0);
   const float* src = x + mat0 * NN;
   float* dst = out + mat0 * NN;
   const int total = nm * NN;
+  auto slot = [](int e) -> int { return (e / NN) * STRIDE + e % NN + (e % NN >= HW ? 1 : 0); };
 
-  // coalesced load of the block's contiguous chunk into the padded layout
-  if (nm == SK_THREADS && (NN % 4) == 0) {
+  // coalesced load of the block's contiguous chunk into the staging layout
+  if (nm == MPB && (HW % 4) == 0) {
     const float4* s4 = reinterpret_cast<const float4*>(src);
-    for (int v = tid; v < total / 4; v += SK_THREADS) {
-      float4 f = __ldcs(s4 + v);
-      int e = v * 4;
-      float* d = sk_smem + (e / NN) * STRIDE + e % NN;
+    for (int q = tid; q < total / 4; q += SK_THREADS) {
+      const float4 f = __ldcs(s4 + q);
+      float* d = sk_smem + slot(q * 4);  // a float4 never straddles a row half
       d[0] = f.x; d[1] = f.y; d[2] = f.z; d[3] = f.w;
     }
   } else {
-    for (int e = tid; e < total; e += SK_THREADS) sk_smem[(e / NN) * STRIDE + e % NN] = __ldcs(src + e);
+    for (int e = tid; e < total; e += SK_THREADS) sk_smem[slot(e)] = __ldcs(src + e);
   }
   __syncthreads();
 
-  if (tid < nm) {
-    const float* my = sk_smem + tid * STRIDE;
-    // K = softmax(x) + eps, kept as column pairs kp[i][c] = (K[i][2c], K[i][2c+1])
-    uint64_t kp[N][C];
+  {
+    // Every thread runs the iteration (the shuffles need all lanes); pairs past the
+    // batch's end work on unused staging slots that are never stored.
+    float* my = sk_smem + ml * STRIDE + h * (HW + 1);
+    const int rot = h * R;  // local column j = global column (j + rot) mod N
+    auto gcol = [&](int j) -> int { return j + rot < N ? j + rot : j + rot - N; };
+    // K = softmax(x) + eps for this thread's rows, as (local) column pairs
+    uint64_t kp[R][C];
     constexpr float kLog2e = 1.4426950408889634f;
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
+    for (int i = 0; i < R; ++i) {
       float r[N];
 #pragma unroll
-      for (int j = 0; j < N; ++j) r[j] = my[i * N + j];
+      for (int j = 0; j < N; ++j) r[j] = my[i * N + gcol(j)];
       float m = r[0];
 #pragma unroll
       for (int j = 1; j < N; ++j) m = fmaxf(m, r[j]);
@@ -269,20 +290,19 @@ __global__ void __launch_bounds__(SK_THREADS)
 #pragma unroll
       for (int c = 0; c < C; ++c) kp[i][c] = sk_pack(fmaf(r[2 * c], rs, eps), fmaf(r[2 * c + 1], rs, eps));
     }
-    float u[N], v[N];
+    float u[R], v[N];  // v in local column order
 #pragma unroll
-    for (int i = 0; i < N; ++i) u[i] = 1.f;
+    for (int i = 0; i < R; ++i) u[i] = 1.f;
 #pragma unroll
     for (int j = 0; j < N; ++j) v[j] = 1.f;
     const int rounds = repeat < 1 ? 1 : repeat;
-    // baseline/sinkhorn.py:15-18: one column pass, then repeat-1 (row, column) pairs
     for (int it = 0; it < rounds; ++it) {
       if (it > 0) {  // row pass: u_i <- u_i / (u_i (K v)_i + eps)
         uint64_t vp[C];
 #pragma unroll
         for (int c = 0; c < C; ++c) vp[c] = sk_pack(v[2 * c], v[2 * c + 1]);
 #pragma unroll
-        for (int i = 0; i < N; ++i) {
+        for (int i = 0; i < R; ++i) {
           uint64_t acc = sk_mul2(kp[i][0], vp[0]);
 #pragma unroll
           for (int c = 1; c < C; ++c) acc = sk_fma2(kp[i][c], vp[c], acc);
@@ -291,7 +311,7 @@ __global__ void __launch_bounds__(SK_THREADS)
           u[i] = u[i] * sk_rcp(fmaf(u[i], lo + hi, eps));
         }
       }
-      // column pass: v_j <- v_j / (v_j (u^T K)_j + eps), two columns at a time
+      // column pass: partial sums of this thread's rows, then v_j <- v_j / (v_j t_j + eps)
       uint64_t t[C];
       {
         const uint64_t u0 = sk_pack(u[0], u[0]);
@@ -299,47 +319,50 @@ __global__ void __launch_bounds__(SK_THREADS)
         for (int c = 0; c < C; ++c) t[c] = sk_mul2(kp[0][c], u0);
       }
 #pragma unroll
-      for (int i = 1; i < N; ++i) {
+      for (int i = 1; i < R; ++i) {
         const uint64_t ui = sk_pack(u[i], u[i]);
 #pragma unroll
         for (int c = 0; c < C; ++c) t[c] = sk_fma2(kp[i][c], ui, t[c]);
       }
+      float tf[N];
 #pragma unroll
-      for (int c = 0; c < C; ++c) {
-        float lo, hi;
-        sk_unpack(t[c], lo, hi);
-        v[2 * c] = v[2 * c] * sk_rcp(fmaf(v[2 * c], lo, eps));
-        v[2 * c + 1] = v[2 * c + 1] * sk_rcp(fmaf(v[2 * c + 1], hi, eps));
+      for (int c = 0; c < C; ++c) sk_unpack(t[c], tf[2 * c], tf[2 * c + 1]);
+      // this thread updates its local columns k < R; the partner sends its partial
+      // sums of them (its local columns R + k) and gets back the new v
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        const float theirs = __shfl_xor_sync(0xFFFFFFFFu, tf[R + k], 1);
+        v[k] = v[k] * sk_rcp(fmaf(v[k], tf[k] + theirs, eps));
       }
+#pragma unroll
+      for (int k = 0; k < R; ++k) v[R + k] = __shfl_xor_sync(0xFFFFFFFFu, v[k], 1);
     }
-    // x_ij = u_i K_ij v_j
+    // x_ij = u_i K_ij v_j for this thread's rows
     uint64_t vp[C];
 #pragma unroll
     for (int c = 0; c < C; ++c) vp[c] = sk_pack(v[2 * c], v[2 * c + 1]);
-    float* myw = sk_smem + tid * STRIDE;
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
+    for (int i = 0; i < R; ++i) {
       const uint64_t ui = sk_pack(u[i], u[i]);
 #pragma unroll
       for (int c = 0; c < C; ++c) {
         float lo, hi;
         sk_unpack(sk_mul2(sk_mul2(kp[i][c], ui), vp[c]), lo, hi);
-        myw[i * N + 2 * c] = lo;
-        myw[i * N + 2 * c + 1] = hi;
+        my[i * N + gcol(2 * c)] = lo;
+        my[i * N + gcol(2 * c + 1)] = hi;
       }
     }
   }
   __syncthreads();
 
-  if (nm == SK_THREADS && (NN % 4) == 0) {
+  if (nm == MPB && (HW % 4) == 0) {
     float4* d4 = reinterpret_cast<float4*>(dst);
-    for (int v = tid; v < total / 4; v += SK_THREADS) {
-      int e = v * 4;
-      const float* s = sk_smem + (e / NN) * STRIDE + e % NN;
-      __stcs(d4 + v, make_float4(s[0], s[1], s[2], s[3]));
+    for (int q = tid; q < total / 4; q += SK_THREADS) {
+      const float* sv = sk_smem + slot(q * 4);
+      __stcs(d4 + q, make_float4(sv[0], sv[1], sv[2], sv[3]));
     }
   } else {
-    for (int e = tid; e < total; e += SK_THREADS) __stcs(dst + e, sk_smem[(e / NN) * STRIDE + e % NN]);
+    for (int e = tid; e < total; e += SK_THREADS) __stcs(dst + e, sk_smem[slot(e)]);
   }
 }
 
