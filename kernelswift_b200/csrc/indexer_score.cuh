@@ -247,6 +247,19 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
       const int nt = ix_item_tiles(p, item, b, g);
       if (nt == 0) continue;
       bool ok = true;
+      // key limits of this warp's tokens (causal: (pos0 + s + 1) / ratio; else T),
+      // fixed for the item, so the division is not repeated per tile
+      int64_t lims[TOK_HALF];
+#pragma unroll
+      for (int u = 0; u < TOK_HALF; ++u) {
+        const int s = g * TOK + half * TOK_HALF + u;
+        int64_t lim = p.T;
+        if (p.causal) {
+          const int64_t l2 = (p.pos0 + s + 1) / p.ratio;
+          lim = l2 < lim ? l2 : lim;
+        }
+        lims[u] = s < p.S ? lim : 0;  // rows past S are not stored
+      }
       for (int t = 0; t < nt; ++t) {
         const int as = ac & 1;
         if (!(ok = mbar_wait_inl(&sh->acc_full[as], (ac >> 1) & 1, wc))) break;
@@ -300,13 +313,8 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int s = u ? s1 : s0;
-            int64_t lim = p.T;
-            if (p.causal) {
-              const int64_t l2 = (p.pos0 + s + 1) / p.ratio;
-              lim = l2 < lim ? l2 : lim;
-            }
             uint16_t out = __bfloat16_as_ushort(__float2bfloat16_rn(u ? acc1 : acc0));
-            if (key >= lim) out = 0xFF80;  // -inf
+            if (key >= lims[jp + u]) out = 0xFF80;  // -inf
             if (s < p.S && key < p.T)
               p.scores[((int64_t)b * p.S + s) * p.score_ld + key] = out;
           }
