@@ -323,6 +323,17 @@ __device__ __forceinline__ void umma_bf16_ss_cg2(uint32_t d_tmem, uint64_t adesc
       : "memory");
 }
 
+// cta_group::2 MMA with descriptors passed as (low, high) words: the start address
+// sits in the low 14 bits, so per-MMA offsets are single 32-bit adds.
+__device__ __forceinline__ void umma_cg2_w(uint32_t d, uint32_t alo, uint32_t ahi, uint32_t blo,
+                                           uint32_t bhi, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{ .reg .pred p; .reg .b64 ad, bd; setp.ne.b32 p, %6, 0; mov.b64 ad, {%1, %2};"
+      " mov.b64 bd, {%3, %4}; tcgen05.mma.cta_group::2.kind::f16 [%0], ad, bd, %5, p; }" ::"r"(d),
+      "r"(alo), "r"(ahi), "r"(blo), "r"(bhi), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
 // Arrive (once) on `bar` when every previously issued tcgen05 op of this thread is done.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(

@@ -342,6 +342,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       };
       if (!v_issuer) {
         const uint64_t qd0 = sdesc_sw128(smem_u32(qs), 16, 1024);
+        const uint32_t qlo = (uint32_t)qd0, qhi = (uint32_t)(qd0 >> 32);
+        const uint32_t rlo = (uint32_t)rd0, rhi = (uint32_t)(rd0 >> 32);
         const uint32_t idesc_s = idesc_bf16_f32(128, SA_NB, false, false);
         for (int j = 0; ok && j < p.nblk; ++j) {
           // S buffer j % 2 was last read by softmax(j - 2)
@@ -357,11 +359,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
             for (int h = 0; h < 2; ++h) {
               if (h == 1 && !two) break;
               const int slh = h ? sl1 : sl0;
-              const uint64_t boff = (uint64_t)(slh * (SA_SLOT >> 4));
+              const uint32_t blo = rlo + (uint32_t)(slh * (SA_SLOT >> 4));
+              const uint32_t alo = qlo + (uint32_t)((d + h) * 512);
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
-                umma_bf16_ss_cg2(d_s, qd0 + (uint64_t)((d + h) * 512 + kk * 2), rd0 + boff + (uint64_t)(kk * 2),
-                                 idesc_s, (d + h > 0 || kk > 0) ? 1u : 0u);
+                umma_cg2_w(d_s, alo + kk * 2, qhi, blo + kk * 2, rhi, idesc_s, (d + h > 0 || kk > 0) ? 1u : 0u);
               umma_commit_cg2(&sh->empty[slh], 3);
               KS_SA_TRACE(12, n + h);
             }
@@ -373,6 +375,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         mbar_wait(&sh->drain_s, 0, wc, false, true);
       } else {
         const uint64_t pd0 = sdesc_sw128(smem_u32(ps), 16, 1024);
+        const uint32_t plo = (uint32_t)pd0, phi = (uint32_t)(pd0 >> 32);
+        const uint32_t rlo = (uint32_t)rd0, rhi = (uint32_t)(rd0 >> 32);
         // (scalars, not arrays: an array indexed in a loop would live in local memory)
         const uint32_t idesc_pv0 = idesc_bf16_f32(128, p.pv_n[0], false, true);
         const uint32_t idesc_pv1 = idesc_bf16_f32(128, p.n_pv > 1 ? p.pv_n[1] : 128, false, true);
@@ -390,18 +394,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
             for (int h = 0; h < 2; ++h) {
               const int sub = sp + h;
               const int slh = h ? sl1 : sl0;
-              const uint64_t boff = (uint64_t)(slh * (SA_SLOT >> 4));
-              const uint64_t ad = pd0 + (uint64_t)((j & 1) * (SA_PBYTES >> 4) + (sub >> 1) * 512 + (sub & 1) * 4);
+              const uint32_t boff = (uint32_t)(slh * (SA_SLOT >> 4));
+              const uint32_t alo = plo + (uint32_t)((j & 1) * (SA_PBYTES >> 4) + (sub >> 1) * 512 + (sub & 1) * 4);
 #pragma unroll
               for (int i = 0; i < 2; ++i) {
                 if (i == 1 && npv < 2) break;
                 // instruction i: N = pv_n[i]; its columns start at segment 2 i (pv_n[0] = 256 when there are two)
                 const uint32_t ocol = tmem + SA_OCOL + (i ? pvn0 / 2 : 0);
-                const uint64_t bd = rd0 + boff + (uint64_t)(i ? (pvn0 / 128) * (SA_VSEG >> 4) : 0);
+                const uint32_t blo = rlo + boff + (uint32_t)(i ? (pvn0 / 128) * (SA_VSEG >> 4) : 0);
 #pragma unroll
                 for (int kk = 0; kk < SA_KC / 16; ++kk)
-                  umma_bf16_ss_cg2(ocol, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 128), i ? idesc_pv1 : idesc_pv0,
-                                   (j > 0 || sub > 0 || kk > 0) ? 1u : 0u);
+                  umma_cg2_w(ocol, alo + kk * 2, phi, blo + kk * 128, rhi, i ? idesc_pv1 : idesc_pv0,
+                             (j > 0 || sub > 0 || kk > 0) ? 1u : 0u);
               }
               umma_commit_cg2(&sh->empty[slh], 3);
               KS_SA_TRACE(12, n + h);
