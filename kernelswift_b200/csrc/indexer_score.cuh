@@ -55,9 +55,15 @@ struct IxShared {
   uint64_t acc_full[2], acc_empty[2];
   uint64_t q_tma[2], q_full[2], q_empty[2];
   uint64_t drain;
+  uint64_t w_full, w_free;  // item weights staged / every epilogue warp done with them
   uint32_t tmem_base;
   int abort;
+  // head weights of the current work item's tokens (token-major, IX_N = tok * H
+  // bf16), staged once per item: read per tile from shared memory rather than
+  // through the global-load path, whose traffic slowed the MMAs
+  alignas(16) uint16_t wbuf[IX_N];
 };
+static_assert(sizeof(IxShared) <= 1024, "IxShared exceeds its 1 KB header");
 
 __device__ __forceinline__ int ix_item_tiles(const IndexerScoreParams& p, int item, int& b,
                                              int& g) {
@@ -105,6 +111,8 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
       mbar_init(&sh->q_empty[i], 1);
     }
     mbar_init(&sh->drain, 1);
+    mbar_init(&sh->w_full, 1);
+    mbar_init(&sh->w_free, IX_EPI_THREADS / 32);
     sh->abort = 0;
     fence_barrier_init();
   }
@@ -241,7 +249,7 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
     const int half = e >> 2;            // which half of the item's tokens
     constexpr int TOK = IX_N / H;
     constexpr int TOK_HALF = TOK / 2;
-    uint32_t ac = 0;
+    uint32_t ac = 0, ic = 0;  // tiles and (non-empty) items so far
     for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
       int b, g;
       const int nt = ix_item_tiles(p, item, b, g);
@@ -260,6 +268,28 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
         }
         lims[u] = s < p.S ? lim : 0;  // rows past S are not stored
       }
+      // stage the item's weights (epilogue warp 0), once every epilogue warp is
+      // done with the previous item's; the others wait until they are in place
+      if (e == 0) {
+        if (ic > 0 && !(ok = mbar_wait(&sh->w_free, (ic - 1) & 1, wc))) break;
+        const int n = lane * 8;  // 8 consecutive weights of token n / H
+        const int u = n / H, h0 = n % H;
+        const int su = g * TOK + u;
+        const uint16_t* src = p.w + (int64_t)b * p.w_bs + (int64_t)(su < p.S ? su : p.S - 1) * H + h0;
+        uint4 v;
+        if (p.w_vec16) {
+          v = __ldg(reinterpret_cast<const uint4*>(src));
+        } else {
+          uint32_t x[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) x[i] = (uint32_t)__ldg(src + 2 * i) | ((uint32_t)__ldg(src + 2 * i + 1) << 16);
+          v = make_uint4(x[0], x[1], x[2], x[3]);
+        }
+        *reinterpret_cast<uint4*>(sh->wbuf + n) = v;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh->w_full);
+      }
+      if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->w_full, ic & 1, wc)))) break;
       for (int t = 0; t < nt; ++t) {
         const int as = ac & 1;
         if (!(ok = mbar_wait_inl(&sh->acc_full[as], (ac >> 1) & 1, wc))) break;
@@ -269,9 +299,9 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
         for (int jp = 0; jp < TOK_HALF; jp += 2) {
           const int j0 = half * TOK_HALF + jp;
           const int s0 = g * TOK + j0, s1 = s0 + 1;
-          // head weights of the two tokens (warp-uniform loads, L1 resident)
-          const uint16_t* wrow0 = p.w + (int64_t)b * p.w_bs + (int64_t)(s0 < p.S ? s0 : p.S - 1) * H;
-          const uint16_t* wrow1 = p.w + (int64_t)b * p.w_bs + (int64_t)(s1 < p.S ? s1 : p.S - 1) * H;
+          // head weights of the two tokens (shared memory, warp-uniform: broadcast)
+          const uint16_t* wrow0 = sh->wbuf + j0 * H;
+          const uint16_t* wrow1 = wrow0 + H;
           const uint32_t col0 = tmem + as * IX_N + j0 * H + ((uint32_t)(quarter * 32) << 16);
           uint64_t acc = 0;  // (token s0, token s1) partial sums, f32x2
 #pragma unroll
@@ -280,21 +310,15 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
             tmem_ld16(col0 + c, r0);
             tmem_ld16(col0 + H + c, r1);
             uint32_t w0[8], w1[8];
-            if (p.w_vec16) {
-              const uint4 a0 = __ldg(reinterpret_cast<const uint4*>(wrow0 + c));
-              const uint4 a1 = __ldg(reinterpret_cast<const uint4*>(wrow0 + c + 8));
-              const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(wrow1 + c));
-              const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(wrow1 + c + 8));
+            {
+              const uint4 a0 = *reinterpret_cast<const uint4*>(wrow0 + c);
+              const uint4 a1 = *reinterpret_cast<const uint4*>(wrow0 + c + 8);
+              const uint4 b0 = *reinterpret_cast<const uint4*>(wrow1 + c);
+              const uint4 b1 = *reinterpret_cast<const uint4*>(wrow1 + c + 8);
               w0[0] = a0.x; w0[1] = a0.y; w0[2] = a0.z; w0[3] = a0.w;
               w0[4] = a1.x; w0[5] = a1.y; w0[6] = a1.z; w0[7] = a1.w;
               w1[0] = b0.x; w1[1] = b0.y; w1[2] = b0.z; w1[3] = b0.w;
               w1[4] = b1.x; w1[5] = b1.y; w1[6] = b1.z; w1[7] = b1.w;
-            } else {
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                w0[i] = __ldg(reinterpret_cast<const uint32_t*>(wrow0 + c) + i);
-                w1[i] = __ldg(reinterpret_cast<const uint32_t*>(wrow1 + c) + i);
-              }
             }
             tmem_wait_ld();
 #pragma unroll
@@ -325,6 +349,9 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
         ++ac;
       }
       if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->w_free);  // this warp is done with the item's weights
+      ++ic;
     }
   }
 
