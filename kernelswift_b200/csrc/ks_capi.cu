@@ -256,7 +256,8 @@ int topk_impl(const void* scores, int64_t score_ld, int64_t B, int64_t S, int64_
   if (B * S > 0x7FFFFFFFll) return fail(KS_ERR_UNSUPPORTED, "topk: too many rows");
   // composites sorted per row: TK_THREADS * ept >= kpow2
   const int ept = kpow2 <= TK_THREADS ? 1 : kpow2 / TK_THREADS;
-  const size_t smem = (size_t)TK_THREADS * ept * 4 + (256 + 256 + TK_WARPS + 4 + 8) * 4 + round_up(T, 8) * 2;
+  const size_t nbuf = (size_t)TK_THREADS * ept > (size_t)TK_HBINS ? (size_t)TK_THREADS * ept : (size_t)TK_HBINS;
+  const size_t smem = nbuf * 4 + (TK_WARPS + 4 + 8 + 2 * TK_WARPS) * 4 + round_up(T, 8) * 2;
   switch (ept) {
     case 1: return launch_topk<1>(p, B * S, smem, st);
     case 2: return launch_topk<2>(p, B * S, smem, st);

@@ -10,11 +10,17 @@
 //
 // One CTA per row.  The valid prefix of the row is staged once in shared memory
 // as 16-bit order keys (monotone in the bf16 value, -0.0 folded onto +0.0).
-//   1. histogram of the high key byte (shared atomics) and a suffix scan find the
-//      byte of the k-th largest key; a second histogram over the low byte, fed
-//      only by the keys of that bucket, gives the exact threshold key `thr`, the
-//      count of keys above it and how many keys equal to it are taken (lowest
-//      indices first);
+//   1. the staging pass also finds the row's smallest and largest key; a
+//      histogram of (key - min) >> s over at most 1024 bins (shared atomics; s = 0
+//      when the row spans at most 1024 distinct keys, as indexer score rows do)
+//      and a descending block scan find the bin of the k-th largest key; when
+//      s > 0 a second histogram over the low s bits, fed only by the keys of that
+//      bin, finishes it.  The result is the exact threshold key `thr`, the count
+//      of keys above it and how many keys equal to it are taken (lowest indices
+//      first).  Bins sized to the row's key range matter: score rows hold a few
+//      hundred distinct bf16 values that nearly all share one high byte, so a
+//      fixed high-byte histogram sends every key of a warp to the same bin and
+//      its atomics serialise;
 //   2. one pass in index order compacts the selected (key, index) pairs with one
 //      block-wide exclusive scan per 4096-element chunk (counts of keys above and
 //      equal to `thr` packed into one word);
@@ -33,6 +39,9 @@ constexpr int TK_THREADS = 512;
 constexpr int TK_WARPS = TK_THREADS / 32;
 constexpr int TK_PER_THREAD = 8;
 constexpr int TK_CHUNK = TK_THREADS * TK_PER_THREAD;
+constexpr int TK_HBITS = 10;                 // first-pass histogram: at most 1024 bins
+constexpr int TK_HBINS = 1 << TK_HBITS;
+constexpr int TK_HPER = TK_HBINS / TK_THREADS;
 
 struct TopkParams {
   const uint16_t* scores;  // bf16 bits, row r at scores + r * row_stride
@@ -85,27 +94,28 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* warp_t
   return res;
 }
 
-// Given a 256-bin histogram, find the bin holding the `need`-th largest element.
-// Writes (bin, count strictly above the bin) to out2.  Uses the first 256 threads.
-__device__ __forceinline__ void find_bin(const uint32_t* hist, uint32_t need, uint32_t* scan,
-                                         uint32_t* out2) {
-  const int t = threadIdx.x;
-  if (t < 256) scan[t] = hist[255 - t];  // descending bin order
-  __syncthreads();
-  for (int o = 1; o < 256; o <<= 1) {
-    uint32_t v = 0;
-    if (t < 256 && t >= o) v = scan[t - o];
-    __syncthreads();
-    if (t < 256) scan[t] += v;
-    __syncthreads();
+// Given a histogram of `nbins` (<= TK_HBINS) bins in ascending key order, find the
+// bin holding the `need`-th largest element (1 <= need <= total count).  Writes
+// (bin, count in the bins above it) to out2.  Thread t scans the bins of
+// descending ranks t * TK_HPER ...; one block scan gives each thread its prefix.
+__device__ __forceinline__ void find_bin_desc(const uint32_t* hist, int nbins, uint32_t need,
+                                              uint32_t* warp_tot, uint32_t* out2) {
+  uint32_t c[TK_HPER], sum = 0;
+#pragma unroll
+  for (int j = 0; j < TK_HPER; ++j) {
+    const int r = threadIdx.x * TK_HPER + j;
+    c[j] = r < nbins ? hist[nbins - 1 - r] : 0u;
+    sum += c[j];
   }
-  if (t < 256) {
-    const uint32_t incl = scan[t];
-    const uint32_t excl = t ? scan[t - 1] : 0;
-    if (incl >= need && excl < need) {
-      out2[0] = 255 - t;
-      out2[1] = excl;
+  uint32_t tot;
+  uint32_t run = block_excl_scan(sum, warp_tot, tot);
+#pragma unroll
+  for (int j = 0; j < TK_HPER; ++j) {
+    if (run < need && run + c[j] >= need) {
+      out2[0] = (uint32_t)(nbins - 1 - (int)(threadIdx.x * TK_HPER + j));
+      out2[1] = run;
     }
+    run += c[j];
   }
   __syncthreads();
 }
@@ -113,14 +123,16 @@ __device__ __forceinline__ void find_bin(const uint32_t* hist, uint32_t need, ui
 template <int EPT>
 __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
   constexpr int NS = TK_THREADS * EPT;  // sorted composites, >= kpow2
+  constexpr int NBUF = NS > TK_HBINS ? NS : TK_HBINS;
   extern __shared__ __align__(16) uint8_t tk_smem[];
-  // layout: sortbuf[NS] u32 | hist[256] | scan[256] | warp_tot[TK_WARPS+4] | misc[8] | keys
+  // layout: sortbuf[NBUF] u32 (the histograms before the compaction) |
+  //         warp_tot[TK_WARPS+4] | misc[8] | red[2*TK_WARPS] | keys
   uint32_t* sortbuf = reinterpret_cast<uint32_t*>(tk_smem);
-  uint32_t* hist = sortbuf + NS;
-  uint32_t* scan = hist + 256;
-  uint32_t* warp_tot = scan + 256;
+  uint32_t* hist = sortbuf;
+  uint32_t* warp_tot = sortbuf + NBUF;
   uint32_t* misc = warp_tot + TK_WARPS + 4;
-  uint16_t* keys = reinterpret_cast<uint16_t*>(misc + 8);
+  uint32_t* red = misc + 8;
+  uint16_t* keys = reinterpret_cast<uint16_t*>(red + 2 * TK_WARPS);
 
   const int tid = threadIdx.x;
   const int64_t row = p.rows - 1 - (int64_t)blockIdx.x;  // longest causal rows first
@@ -132,11 +144,9 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
   const int K = p.k;
   const uint16_t* src = p.scores + row * p.row_stride;
 
-  if (tid < 256) hist[tid] = 0;
-  __syncthreads();
-
-  // ---- stage the valid prefix as order keys, histogram of the high byte
+  // ---- stage the valid prefix as order keys; smallest and largest key
   const bool need_select = L > K;
+  uint32_t kmin = 0xFFFFu, kmax = 0u;
   for (int base = 0; base < L; base += TK_CHUNK) {
     const int i0 = base + tid * TK_PER_THREAD;
     uint32_t kv[TK_PER_THREAD];
@@ -154,9 +164,10 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
       o.z = kv[4] | (kv[5] << 16);
       o.w = kv[6] | (kv[7] << 16);
       *reinterpret_cast<uint4*>(keys + i0) = o;
-      if (need_select) {
 #pragma unroll
-        for (int q = 0; q < TK_PER_THREAD; ++q) atomicAdd(hist + (kv[q] >> 8), 1u);
+      for (int q = 0; q < TK_PER_THREAD; ++q) {
+        kmin = min(kmin, kv[q]);
+        kmax = max(kmax, kv[q]);
       }
     } else {
 #pragma unroll
@@ -164,20 +175,34 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
         if (i0 + q < L) {
           kv[q] = bf16_key(src[i0 + q]);
           keys[i0 + q] = (uint16_t)kv[q];
-          if (need_select) atomicAdd(hist + (kv[q] >> 8), 1u);
+          kmin = min(kmin, kv[q]);
+          kmax = max(kmax, kv[q]);
         }
       }
     }
   }
-  __syncthreads();
 
   uint32_t thr = 0, need_eq = 0;
-  if (need_select) {
-    find_bin(hist, (uint32_t)K, scan, misc);
-    const uint32_t b1 = misc[0], above1 = misc[1];
-    if (tid < 256) hist[tid] = 0;
-    __syncthreads();
-    // low-byte histogram of the keys in bucket b1 only
+  if (need_select) {  // block-uniform
+    const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+    for (int j = 0; j < TK_HPER; ++j) hist[tid * TK_HPER + j] = 0u;
+    kmin = __reduce_min_sync(0xFFFFFFFFu, kmin);
+    kmax = __reduce_max_sync(0xFFFFFFFFu, kmax);
+    if (lane == 0) {
+      red[warp] = kmin;
+      red[TK_WARPS + warp] = kmax;
+    }
+    __syncthreads();  // also publishes the staged keys and the cleared bins
+#pragma unroll
+    for (int w = 0; w < TK_WARPS; ++w) {
+      kmin = min(kmin, red[w]);
+      kmax = max(kmax, red[TK_WARPS + w]);
+    }
+    // bins of width 2^sh cover [kmin, kmax] in at most TK_HBINS bins
+    const uint32_t range = kmax - kmin;
+    const int bits = range ? 32 - __clz(range) : 0;
+    const int sh = bits > TK_HBITS ? bits - TK_HBITS : 0;
     for (int base = 0; base < L; base += TK_CHUNK) {
       const int i0 = base + tid * TK_PER_THREAD;
       if (i0 + TK_PER_THREAD <= L) {
@@ -185,23 +210,52 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          if (((w[q] >> 8) & 0xFFu) == b1) atomicAdd(hist + (w[q] & 0xFFu), 1u);
-          if ((w[q] >> 24) == b1) atomicAdd(hist + ((w[q] >> 16) & 0xFFu), 1u);
+          atomicAdd(hist + (((w[q] & 0xFFFFu) - kmin) >> sh), 1u);
+          atomicAdd(hist + (((w[q] >> 16) - kmin) >> sh), 1u);
         }
       } else {
-        for (int q = 0; q < TK_PER_THREAD; ++q) {
-          if (i0 + q < L) {
-            const uint32_t key = keys[i0 + q];
-            if ((key >> 8) == b1) atomicAdd(hist + (key & 0xFFu), 1u);
-          }
-        }
+        for (int q = 0; q < TK_PER_THREAD; ++q)
+          if (i0 + q < L) atomicAdd(hist + (((uint32_t)keys[i0 + q] - kmin) >> sh), 1u);
       }
     }
     __syncthreads();
-    find_bin(hist, (uint32_t)K - above1, scan, misc + 2);
-    const uint32_t b2 = misc[2], above2 = misc[3];
-    thr = (b1 << 8) | b2;
+    find_bin_desc(hist, (int)(range >> sh) + 1, (uint32_t)K, warp_tot, misc);
+    const uint32_t b1 = misc[0], above1 = misc[1];
+    uint32_t b2 = 0, above2 = 0;
+    if (sh > 0) {
+      // the low sh bits of the keys in bin b1 only
+      const uint32_t lmask = (1u << sh) - 1u;
+      if (tid < (1 << sh)) hist[tid] = 0u;
+      __syncthreads();
+      for (int base = 0; base < L; base += TK_CHUNK) {
+        const int i0 = base + tid * TK_PER_THREAD;
+        if (i0 + TK_PER_THREAD <= L) {
+          const uint4 v = *reinterpret_cast<const uint4*>(keys + i0);
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t d0 = (w[q] & 0xFFFFu) - kmin, d1 = (w[q] >> 16) - kmin;
+            if ((d0 >> sh) == b1) atomicAdd(hist + (d0 & lmask), 1u);
+            if ((d1 >> sh) == b1) atomicAdd(hist + (d1 & lmask), 1u);
+          }
+        } else {
+          for (int q = 0; q < TK_PER_THREAD; ++q) {
+            if (i0 + q < L) {
+              const uint32_t d = (uint32_t)keys[i0 + q] - kmin;
+              if ((d >> sh) == b1) atomicAdd(hist + (d & lmask), 1u);
+            }
+          }
+        }
+      }
+      __syncthreads();
+      find_bin_desc(hist, 1 << sh, (uint32_t)K - above1, warp_tot, misc + 2);
+      b2 = misc[2];
+      above2 = misc[3];
+    }
+    thr = kmin + (b1 << sh) + b2;
     need_eq = (uint32_t)K - above1 - above2;
+  } else {
+    __syncthreads();  // publishes the staged keys
   }
 
   // ---- compaction in index order: one scan of (equal << 16 | above) counts per chunk
