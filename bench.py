@@ -582,8 +582,18 @@ class Timers:
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
+    """nvidia-smi samples of the GPU that `index` names in this process.  The GPU is
+    named to nvidia-smi by its UUID: a CUDA index can differ from nvidia-smi's when
+    CUDA_VISIBLE_DEVICES remaps the devices."""
+
     def __init__(self, index):
+        import torch
+
         self.index = index
+        try:
+            self.gpu_id = "GPU-" + str(torch.cuda.get_device_properties(index).uuid)
+        except (AttributeError, RuntimeError):
+            self.gpu_id = str(index)
         self.proc = None
         self.path = None
 
@@ -595,7 +605,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None

@@ -24,7 +24,8 @@
 //   2. one pass in index order compacts the selected (key, index) pairs with one
 //      block-wide exclusive scan per 4096-element chunk (counts of keys above and
 //      equal to `thr` packed into one word);
-//   3. a bitonic sort of the 32-bit composites ((0xFFFF-key)<<16 | index) puts
+//   3. a stable counting sort when the selected keys span at most 128 values (see
+//      below), else a bitonic sort of the 32-bit composites ((0xFFFF-key)<<16 | index) puts
 //      them in (value desc, index asc) order; the composites are all distinct.
 //      Each thread holds EPT consecutive composites in registers: strides below
 //      EPT are exchanged in registers, strides within a warp by shuffles, and only
@@ -42,6 +43,7 @@ constexpr int TK_CHUNK = TK_THREADS * TK_PER_THREAD;
 constexpr int TK_HBITS = 10;                 // first-pass histogram: at most 1024 bins
 constexpr int TK_HBINS = 1 << TK_HBITS;
 constexpr int TK_HPER = TK_HBINS / TK_THREADS;
+constexpr int TK_CBINS = 128;                // counting sort: at most 128 distinct keys
 
 struct TopkParams {
   const uint16_t* scores;  // bf16 bits, row r at scores + r * row_stride
@@ -182,23 +184,27 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
     }
   }
 
-  uint32_t thr = 0, need_eq = 0;
-  if (need_select) {  // block-uniform
-    const int lane = tid & 31, warp = tid >> 5;
+  // the row's smallest and largest key (for the threshold bins and the counting sort)
+  const int lane = tid & 31, warp = tid >> 5;
+  if (need_select) {
 #pragma unroll
     for (int j = 0; j < TK_HPER; ++j) hist[tid * TK_HPER + j] = 0u;
-    kmin = __reduce_min_sync(0xFFFFFFFFu, kmin);
-    kmax = __reduce_max_sync(0xFFFFFFFFu, kmax);
-    if (lane == 0) {
-      red[warp] = kmin;
-      red[TK_WARPS + warp] = kmax;
-    }
-    __syncthreads();  // also publishes the staged keys and the cleared bins
+  }
+  kmin = __reduce_min_sync(0xFFFFFFFFu, kmin);
+  kmax = __reduce_max_sync(0xFFFFFFFFu, kmax);
+  if (lane == 0) {
+    red[warp] = kmin;
+    red[TK_WARPS + warp] = kmax;
+  }
+  __syncthreads();  // also publishes the staged keys and the cleared bins
 #pragma unroll
-    for (int w = 0; w < TK_WARPS; ++w) {
-      kmin = min(kmin, red[w]);
-      kmax = max(kmax, red[TK_WARPS + w]);
-    }
+  for (int w = 0; w < TK_WARPS; ++w) {
+    kmin = min(kmin, red[w]);
+    kmax = max(kmax, red[TK_WARPS + w]);
+  }
+
+  uint32_t thr = 0, need_eq = 0;
+  if (need_select) {  // block-uniform
     // bins of width 2^sh cover [kmin, kmax] in at most TK_HBINS bins
     const uint32_t range = kmax - kmin;
     const int bits = range ? 32 - __clz(range) : 0;
@@ -254,8 +260,6 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
     }
     thr = kmin + (b1 << sh) + b2;
     need_eq = (uint32_t)K - above1 - above2;
-  } else {
-    __syncthreads();  // publishes the staged keys
   }
 
   // ---- compaction in index order: one scan of (equal << 16 | above) counts per chunk
@@ -306,6 +310,75 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
   for (int i = nsel + tid; i < NS; i += TK_THREADS) sortbuf[i] = 0xFFFFFFFFu;
   __syncthreads();
 
+  // output slot i: the selected element `comp` (valid) or -1
+  auto write_out = [&](int i, bool valid, uint32_t comp) {
+    int64_t o = -1;
+    if (valid) {
+      const int64_t idx = (int64_t)(comp & 0xFFFFu);
+      o = (p.causal && idx >= lim64) ? -1 : idx + p.offset;
+    }
+    if (p.out_i64)
+      reinterpret_cast<int64_t*>(p.out)[row * p.out_row_stride + i] = o;
+    else
+      reinterpret_cast<int32_t*>(p.out)[row * p.out_row_stride + i] = (int32_t)o;
+  };
+
+  // ---- stable counting sort when the selected keys span at most TK_CBINS values
+  // (indexer score rows: a few dozen).  sortbuf holds the selection in index order;
+  // warp w ranks its contiguous segment.  Equal keys of one 32-element step are
+  // found with match_any and ranked by lane, so every element's output position is
+  // (elements of larger keys) + (equal keys in earlier warps, steps and lanes): value
+  // descending, index ascending, as the bitonic sort below gives.  The per-warp
+  // counters live in the staged-key area, which the compaction has finished with.
+  {
+    const uint32_t lo = need_select ? thr : kmin;
+    const bool use_count = nsel > 0 && kmax - lo < (uint32_t)TK_CBINS &&
+                           (size_t)((p.T + 7) & ~7) * 2 >= (size_t)TK_WARPS * TK_CBINS * 2;
+    if (use_count) {  // block-uniform
+      uint16_t* cnt = keys;  // [TK_WARPS][TK_CBINS]
+      for (int i = tid; i < TK_WARPS * TK_CBINS; i += TK_THREADS) cnt[i] = 0;
+      __syncthreads();
+      const int seg = (nsel + TK_THREADS - 1) / TK_THREADS * 32;
+      const int s0 = warp * seg, s1 = min(nsel, s0 + seg);
+      uint16_t* wc = cnt + warp * TK_CBINS;
+      for (int b = s0; b < s1; b += 32) {
+        const int i = b + lane;
+        const uint32_t d = i < s1 ? kmax - (0xFFFFu - (sortbuf[i] >> 16)) : 0xFFFFFFFFu;
+        const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
+        if (i < s1 && lane == __ffs(peers) - 1) wc[d] += (uint16_t)__popc(peers);
+        __syncwarp();
+      }
+      __syncthreads();
+      // exclusive prefix over warps per key, then over keys (descending key = ascending d)
+      uint32_t tot_b = 0;
+      if (tid < TK_CBINS) {
+        for (int w = 0; w < TK_WARPS; ++w) {
+          const uint32_t c = cnt[w * TK_CBINS + tid];
+          cnt[w * TK_CBINS + tid] = (uint16_t)tot_b;
+          tot_b += c;
+        }
+      }
+      uint32_t total;
+      const uint32_t kbase = block_excl_scan(tid < TK_CBINS ? tot_b : 0u, warp_tot, total);
+      if (tid < TK_CBINS)
+        for (int w = 0; w < TK_WARPS; ++w) cnt[w * TK_CBINS + tid] += (uint16_t)kbase;
+      __syncthreads();
+      const uint32_t lt = (1u << lane) - 1u;
+      for (int b = s0; b < s1; b += 32) {
+        const int i = b + lane;
+        const uint32_t comp = i < s1 ? sortbuf[i] : 0u;
+        const uint32_t d = i < s1 ? kmax - (0xFFFFu - (comp >> 16)) : 0xFFFFFFFFu;
+        const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
+        if (i < s1) write_out((int)wc[d] + __popc(peers & lt), true, comp);
+        __syncwarp();
+        if (i < s1 && lane == __ffs(peers) - 1) wc[d] += (uint16_t)__popc(peers);
+        __syncwarp();
+      }
+      for (int i = nsel + tid; i < K; i += TK_THREADS) write_out(i, false, 0u);
+      return;
+    }
+  }
+
   // ---- bitonic sort of NS composites, ascending; thread t owns elements t*EPT ..
   uint32_t v[EPT];
 #pragma unroll
@@ -353,17 +426,7 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
 #pragma unroll
   for (int q = 0; q < EPT; ++q) {
     const int i = tid * EPT + q;
-    if (i < K) {
-      int64_t o = -1;
-      if (i < nsel) {
-        const int64_t idx = (int64_t)(v[q] & 0xFFFFu);
-        o = (p.causal && idx >= lim64) ? -1 : idx + p.offset;
-      }
-      if (p.out_i64)
-        reinterpret_cast<int64_t*>(p.out)[row * p.out_row_stride + i] = o;
-      else
-        reinterpret_cast<int32_t*>(p.out)[row * p.out_row_stride + i] = (int32_t)o;
-    }
+    if (i < K) write_out(i, i < nsel, v[q]);
   }
 }
 
