@@ -55,7 +55,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, uint32_t cta) {
   asm volatile(
       "{ .reg .b32 ra; mapa.shared::cluster.u32 ra, %0, %1;"
-      " mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra]; }" ::"r"(smem_u32(bar)),
+      " mbarrier.arrive.shared::cluster.b64 _, [ra]; }" ::"r"(smem_u32(bar)),
       "r"(cta)
       : "memory");
 }
