@@ -47,6 +47,16 @@ def measured_peaks():
             "source": "fallback"}
 
 
+# DRAM bytes (read + write) per query token of the sparse-attention kernel at the
+# H=128, D=576, dv=512, N=32768, K=2048 geometry, from an ncu capture of one full C4
+# launch (dram__bytes_read.sum + dram__bytes_write.sum = 5.102e9 B for 16384 tokens,
+# `ncu --metrics ... -k regex:sparse_attn -s 3 -c 1 python bench.py --workload c4`).
+# The kernel's traffic grows with the tokens it
+# processes (q in, out back, the kv rows of a batch from L2), so a launch's traffic
+# is this figure times its tokens.
+SA_DRAM_BYTES_PER_TOKEN_MLA = 5.102018560e9 / 16384
+
+
 # ---------------------------------------------------------------- workloads
 class Workload:
     name = ""
@@ -68,6 +78,10 @@ class Workload:
 
     def e2e_note(self):
         return "copy-in, ops and copy-out in order on the current stream"
+
+    def traffic(self, kernel):
+        """DRAM bytes per step of `kernel` (scaled from an ncu capture), or None."""
+        return None
 
 
 def _freqs(S, rd, pos0=0):
@@ -150,6 +164,11 @@ class DsaE2E(Workload):
 
     def launches_per_step(self):
         return 3 * len(self.ranges) + 1  # (score + top-k + attention) per range, Sinkhorn
+
+    def traffic(self, kernel):
+        if kernel != "sparse_attn" or (self.H_sa, self.D_sa, self.dv, self.k) != (128, 576, 512, 2048):
+            return None
+        return SA_DRAM_BYTES_PER_TOKEN_MLA * self.B * sum(b - a for a, b in self.ranges)
 
     def host_buffers(self):
         import torch
@@ -396,6 +415,11 @@ class SparseAttnOp(SingleOp):
 
     def work(self):
         return {"sparse_attn": 2 * self.B * self.rows * self.H * self.K * (self.D + self.dv)}, "tensor"
+
+    def traffic(self, kernel):
+        if self.cfg != "c4" or kernel != "sparse_attn":
+            return None
+        return SA_DRAM_BYTES_PER_TOKEN_MLA * self.B * self.rows
 
     def run(self, timers=None):
         from kernelswift_b200 import ops
@@ -750,7 +774,7 @@ def main():
         ach = work[dom] / (spans[dom] / 1e3) / 1e9
         peak, unit, src = peaks["hbm_gbs"], "GB/s", "HBM copy"
     roofline = {"bound": bound, "kernel": dom, "achieved": round(ach, 1), "peak": peak,
-                "unit": unit, "frac": round(ach / peak, 4), "traffic": None,
+                "unit": unit, "frac": round(ach / peak, 4), "traffic": wl.traffic(dom),
                 "algorithmic_per_step": work[dom],
                 "peak_source": f"{peaks['source']} ({src})",
                 "per_kernel_ms": {k: round(v, 4) for k, v in spans.items()}}
