@@ -28,9 +28,13 @@ def contiguous(n: int, world: int, rank: int) -> list[tuple[int, int]]:
 
 
 def zigzag(n: int, world: int, rank: int) -> list[tuple[int, int]]:
+    """Rank r's causal rows: chunks r and 2*world-1-r of 2*world; the two are one
+    range when they touch (world == 1), so a single rank runs one call per op."""
     chunks = contiguous_chunks(n, 2 * world)
-    out = [chunks[rank], chunks[2 * world - 1 - rank]]
-    return [c for c in out if c[1] > c[0]]
+    out = [c for c in (chunks[rank], chunks[2 * world - 1 - rank]) if c[1] > c[0]]
+    if len(out) == 2 and out[0][1] == out[1][0]:
+        out = [(out[0][0], out[1][1])]
+    return out
 
 
 def contiguous_chunks(n: int, parts: int) -> list[tuple[int, int]]:

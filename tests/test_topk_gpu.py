@@ -72,3 +72,28 @@ def test_dsa_prefill_shape(cuda_ok):
     ops.device_status()
     ref = oracle_topk(sc, T, 2048, 1, True, 0, 0)
     assert np.array_equal(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("spread", ["narrow", "wide"])
+def test_counting_and_bitonic_sort_paths(cuda_ok, spread):
+    """The kernel sorts a row's selection with a stable counting sort when the
+    selected keys span at most 128 bf16 values and with a bitonic sort otherwise;
+    both must give the stable oracle's order.  Narrow rows mimic indexer scores
+    (values in [1.5, 2.5): about 100 distinct bf16 keys, heavy ties); wide rows
+    spread over many exponents, so the selection spans thousands of keys."""
+    from kernelswift_b200 import ops
+
+    B, S, T, k = 1, 64, 6000, 2048
+    rng = np.random.default_rng(11 if spread == "narrow" else 12)
+    if spread == "narrow":
+        x = rng.uniform(1.5, 2.5, (B, S, T)).astype(np.float32)
+    else:
+        x = (rng.standard_normal((B, S, T)) * np.exp2(rng.integers(-20, 20, (B, S, T)))).astype(np.float32)
+    sc = O.f32_to_bf16(x)
+    span = len(np.unique(np.sort(sc[0, 0].view(np.int16).astype(np.int64))[-k:]))
+    assert (span <= 128) == (spread == "narrow")
+    for dtype in (torch.int32, torch.int64):
+        out = ops.topk_rows(bf16_from_bits(sc), T, k, 1, True, 3, 4000, dtype)
+        ops.device_status()
+        ref = oracle_topk(sc, T, k, 1, True, 3, 4000)
+        assert np.array_equal(out.cpu().numpy().astype(np.int64), ref)
