@@ -317,19 +317,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       // Descriptors are built once; a byte offset o moves the start address field by o / 16.
       const uint64_t rd0 = sdesc_sw128(smem_u32(smem + p.r_off), v_issuer ? SA_VSEG : 16, 1024);
       uint32_t ph = 0;  // bit k: parity of the next phase of slot k's full barrier for this stream
-      // ring position of (block j, chunk c) of this stream
-      auto pos = [&](int j, int c) -> uint32_t {
-        if (!v_issuer) return j == 0 ? (uint32_t)c : (uint32_t)(nkb + (j - 1) * (nkb + SA_NKC) + c);
-        return (uint32_t)(nkb + j * (nkb + SA_NKC) + (j + 1 < p.nblk ? nkb : 0) + c);
+      // Ring position (rn) and slot (rs = rn mod n_slots) of this stream's next
+      // chunk, advanced incrementally: this thread's per-chunk work is a short
+      // dependent chain, so it carries no division.  Ring order S(0) | S(1) V(0) |
+      // S(2) V(1) | ... | V(nblk-1): the QK stream starts at 0 and skips V(j-2)
+      // before S(j), j >= 2; the V stream starts after S(1) and skips S(j+2) after V(j).
+      const int ns = p.n_slots;
+      uint32_t rn = v_issuer ? (uint32_t)(nkb + (p.nblk > 1 ? nkb : 0)) : 0u;
+      int rs = (int)(rn % (uint32_t)ns);
+      auto adv = [&](int k) {
+        rn += (uint32_t)k;
+        rs += k;
+        while (rs >= ns) rs -= ns;
       };
       // Chunks are taken two at a time (ring positions n, n + 1): both barriers
       // are probed before either result is needed, so one probe latency covers
       // eight MMAs.
       uint64_t* const fulls = v_issuer ? sh->full_v : sh->full_s;
-      auto take2 = [&](uint32_t n, bool two, int& s0, int& s1) -> bool {
+      auto take2 = [&](uint32_t n, int s0, bool two, int& s1) -> bool {
         wc.tag = (int)n;
-        s0 = (int)(n % (uint32_t)p.n_slots);
-        s1 = s0 + 1 == p.n_slots ? 0 : s0 + 1;
+        s1 = s0 + 1 == ns ? 0 : s0 + 1;
         const uint32_t b0 = smem_u32(&fulls[s0]), b1 = smem_u32(&fulls[s1]);
         const uint32_t q0 = (ph >> s0) & 1u, q1 = (ph >> s1) & 1u;
         bool r0 = mbar_poll(b0, q0);
@@ -350,11 +357,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
           wc.tag = 2000 + j;
           if (j >= 2 && !(ok = mbar_wait_inl(&sh->s_free[j & 1], ((j - 2) >> 1) & 1, wc))) break;
           const uint32_t d_s = tmem + (j & 1) * SA_SCOLS;
+          if (j >= 2) adv(SA_NKC);
           for (int d = 0; d < nkb; d += 2) {
-            const uint32_t n = pos(j, d);
+            const uint32_t n = rn;
             const bool two = d + 1 < nkb;
-            int sl0, sl1;
-            if (!(ok = take2(n, two, sl0, sl1))) break;
+            const int sl0 = rs;
+            int sl1;
+            if (!(ok = take2(n, sl0, two, sl1))) break;
+            adv(two ? 2 : 1);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               if (h == 1 && !two) break;
@@ -387,9 +397,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
           if (!(ok = mbar_wait_inl(&sh->p_full[j & 1], (j >> 1) & 1, wc))) break;
           KS_SA_TRACE(8, j);
           for (int sp = 0; sp < SA_NKC; sp += 2) {
-            const uint32_t n = pos(j, sp);
-            int sl0, sl1;
-            if (!(ok = take2(n, true, sl0, sl1))) break;
+            const uint32_t n = rn;
+            const int sl0 = rs;
+            int sl1;
+            if (!(ok = take2(n, sl0, true, sl1))) break;
+            adv(2);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int sub = sp + h;
@@ -413,6 +425,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
           }
           if (!ok) break;
           umma_commit_cg2(&sh->p_free[j & 1], 3);
+          if (j + 2 < p.nblk) adv(nkb);
         }
         if (ok) umma_commit_cg2(&sh->o_full, 3);
         umma_commit_cg2(&sh->drain_v, 1);
