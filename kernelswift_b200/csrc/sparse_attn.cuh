@@ -330,22 +330,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         rs += k;
         while (rs >= ns) rs -= ns;
       };
-      // Chunks are taken two at a time (ring positions n, n + 1): both barriers
-      // are probed before either result is needed, so one probe latency covers
-      // eight MMAs.
       uint64_t* const fulls = v_issuer ? sh->full_v : sh->full_s;
-      auto take2 = [&](uint32_t n, int s0, bool two, int& s1) -> bool {
+      // One chunk at a time: its MMAs go out as soon as it has landed, so its slot
+      // is released without waiting for the next chunk (the kernel is bound by how
+      // fast slots turn over; taking chunks in pairs held each first chunk back).
+      auto take1 = [&](uint32_t n, int s0) -> bool {
         wc.tag = (int)n;
-        s1 = s0 + 1 == ns ? 0 : s0 + 1;
-        const uint32_t b0 = smem_u32(&fulls[s0]), b1 = smem_u32(&fulls[s1]);
-        const uint32_t q0 = (ph >> s0) & 1u, q1 = (ph >> s1) & 1u;
-        bool r0 = mbar_poll(b0, q0);
-        bool r1 = !two || mbar_poll(b1, q1);
+        const uint32_t q0 = (ph >> s0) & 1u;
+        bool r0 = mbar_poll(smem_u32(&fulls[s0]), q0);
         if (!r0) r0 = mbar_wait_inl(&fulls[s0], q0, wc);
-        if (r0 && !r1) r1 = mbar_wait_inl(&fulls[s1], q1, wc);
-        ph ^= (1u << s0) | (two ? 1u << s1 : 0u);
+        ph ^= 1u << s0;
         tc_fence_after();
-        return r0 && r1;
+        return r0;
       };
       if (!v_issuer) {
         const uint64_t qd0 = sdesc_sw128(smem_u32(qs), 16, 1024);
@@ -358,25 +354,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
           if (j >= 2 && !(ok = mbar_wait_inl(&sh->s_free[j & 1], ((j - 2) >> 1) & 1, wc))) break;
           const uint32_t d_s = tmem + (j & 1) * SA_SCOLS;
           if (j >= 2) adv(SA_NKC);
-          for (int d = 0; d < nkb; d += 2) {
+          for (int d = 0; d < nkb; ++d) {
             const uint32_t n = rn;
-            const bool two = d + 1 < nkb;
-            const int sl0 = rs;
-            int sl1;
-            if (!(ok = take2(n, sl0, two, sl1))) break;
-            adv(two ? 2 : 1);
+            const int slh = rs;
+            if (!(ok = take1(n, slh))) break;
+            adv(1);
+            const uint32_t blo = rlo + (uint32_t)(slh * (SA_SLOT >> 4));
+            const uint32_t alo = qlo + (uint32_t)(d * 512);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              if (h == 1 && !two) break;
-              const int slh = h ? sl1 : sl0;
-              const uint32_t blo = rlo + (uint32_t)(slh * (SA_SLOT >> 4));
-              const uint32_t alo = qlo + (uint32_t)((d + h) * 512);
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                umma_cg2_w(d_s, alo + kk * 2, qhi, blo + kk * 2, rhi, idesc_s, (d + h > 0 || kk > 0) ? 1u : 0u);
-              umma_commit_cg2(&sh->empty[slh], 3);
-              KS_SA_TRACE(12, n + h);
-            }
+            for (int kk = 0; kk < 4; ++kk)
+              umma_cg2_w(d_s, alo + kk * 2, qhi, blo + kk * 2, rhi, idesc_s, (d > 0 || kk > 0) ? 1u : 0u);
+            umma_commit_cg2(&sh->empty[slh], 3);
+            KS_SA_TRACE(12, n);
           }
           if (!ok) break;
           umma_commit_cg2(&sh->acc_full[j & 1], 3);
@@ -397,15 +386,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
           if (!(ok = mbar_wait_inl(&sh->p_full[j & 1], (j >> 1) & 1, wc))) break;
           KS_SA_TRACE(8, j);
           for (int sp = 0; sp < SA_NKC; sp += 2) {
-            const uint32_t n = rn;
-            const int sl0 = rs;
-            int sl1;
-            if (!(ok = take2(n, sl0, true, sl1))) break;
-            adv(2);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int sub = sp + h;
-              const int slh = h ? sl1 : sl0;
+              const uint32_t n = rn;
+              const int slh = rs;
+              if (!(ok = take1(n, slh))) break;
+              adv(1);
               const uint32_t boff = (uint32_t)(slh * (SA_SLOT >> 4));
               const uint32_t alo = plo + (uint32_t)((j & 1) * (SA_PBYTES >> 4) + (sub >> 1) * 512 + (sub & 1) * 4);
 #pragma unroll
@@ -420,8 +407,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
                              (j > 0 || sub > 0 || kk > 0) ? 1u : 0u);
               }
               umma_commit_cg2(&sh->empty[slh], 3);
-              KS_SA_TRACE(12, n + h);
+              KS_SA_TRACE(12, n);
             }
+            if (!ok) break;
           }
           if (!ok) break;
           umma_commit_cg2(&sh->p_free[j & 1], 3);
