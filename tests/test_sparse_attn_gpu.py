@@ -107,6 +107,27 @@ def test_edge_rows(cuda_ok):
     assert torch.allclose(o[0, 2], kv[0, idx[0, 2, 0]].float().expand(H, D), atol=1e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize("D,dv", [(576, 512), (128, 128)])
+def test_trailing_invalid_blocks(cuda_ok, D, dv):
+    """Rows whose indices are valid only in a prefix (the indexer's output for early
+    causal rows: -1 after the first s + 1 entries).  The kernel stops after the last
+    256-key block holding a valid index; prefixes ending on, just before and just after
+    block boundaries, a single entry and none must match the oracle."""
+    from kernelswift_b200 import ops
+
+    B, H, N, K = 1, 128 if D == 576 else 16, 3000, 1024
+    lens = [0, 1, 255, 256, 257, 511, 512, 700, 1023, 1024]
+    M = len(lens)
+    q, kv, s, idx = make_case(B, M, H, D, N, K, seed=21)
+    for m, n in enumerate(lens):
+        idx[0, m, n:] = -1
+    out = ops.sparse_attn(q.cuda(), kv.cuda(), s.cuda(), idx.cuda(), D ** -0.5, dv)
+    ops.device_status()
+    ref = O.sparse_attn(bits_from_bf16(q), bits_from_bf16(kv), s.numpy(), idx.numpy(), D ** -0.5, dv)
+    assert_close(bits_from_bf16(out), ref)
+    assert torch.all(out[0, 0].float() == 0)
+
+
 def test_mla_scale_rows(cuda_ok):
     """C4 geometry (4, 4096, 128, 576), N = 32768, K = 2048, dv = 512, causal-valid
     indices; the oracle checks a sample of rows."""
