@@ -200,11 +200,11 @@ class DsaE2E(Workload):
                         return t[i][bb:bb + 1, r0:r1]
 
                     def launch(i=i, bb=bb, r0=r0, r1=r1, a=a, sl=sl):
-                        ops.indexer_topk(sl(self.q_ix), self.k_ix[bb:bb + 1], sl(self.w),
-                                         self.freqs[i][r0:r1], self.rd, self.S, self.k, 1, True, 0,
-                                         pos0=a + r0, out=sl(self.idx), workspace=self.ws)
-                        ops.sparse_attn(sl(self.q_sa), self.kv[bb:bb + 1], self.sink, sl(self.idx),
-                                        self.D_sa ** -0.5, self.dv, out=sl(self.out))
+                        # the whole indexer -> sparse attention step in one library call
+                        ops.dsa(sl(self.q_ix), self.k_ix[bb:bb + 1], sl(self.w), self.freqs[i][r0:r1],
+                                self.rd, self.S, self.k, sl(self.q_sa), self.kv[bb:bb + 1],
+                                self.sink, self.D_sa ** -0.5, self.dv, 1, True, 0, pos0=a + r0,
+                                out=sl(self.out), idx_out=sl(self.idx), workspace=self.ws)
 
                     ins = [(sl(self.q_ix), sl(h["q_ix"])), (sl(self.w), sl(h["w"])),
                            (sl(self.q_sa), sl(h["q_sa"]))]
@@ -230,8 +230,9 @@ class DsaE2E(Workload):
 
     def e2e_note(self):
         return (f"{len(self._pipeline().pieces)} pieces per step (<= 4096 query rows each): "
-                "host->device copies, the ops and device->host copies on three streams, piece by "
-                "piece, so copies in both directions overlap the kernels and each other")
+                "host->device copies, the ops (ops.dsa: indexer -> sparse attention in one library "
+                "call; ops.sinkhorn) and device->host copies on three streams, piece by piece, so "
+                "copies in both directions overlap the kernels and each other")
 
     def e2e_bytes(self):
         nb = lambda ts: sum(t.numel() * t.element_size() for t in ts)
@@ -677,9 +678,114 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-per-op", action="store_true",
+                    help="skip the per-operator block of the default workload's line")
     ap.add_argument("--tokens", type=int, default=None,
                     help="query rows per batch (small cases for profiling; not a bench line)")
     return ap.parse_args()
+
+
+def timed_region(wl, steps, world, local, device, barrier):
+    """Time `steps` device-resident steps of `wl` (already warmed up): CUDA events on
+    the current stream around the whole loop, bracketed by a barrier and a device
+    synchronize on both sides, max over ranks; per-kernel spans; the SM clocks
+    sampled meanwhile.  Returns (ms per step, spans, clocks, ms with the flush):
+    for workloads that flush L2 between steps the step time is the sum of the op
+    spans and the whole-loop time (flush included) is returned beside it."""
+    import torch
+    import torch.distributed as dist
+    from kernelswift_b200 import ops
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    timers = Timers()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        wl.run(timers)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / steps
+    clk = clocks.stop()
+    ops.device_status()
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    spans = timers.per_step_ms(steps)
+    ms_with_flush = None
+    if wl.flushes:
+        ms_with_flush = ms
+        t = torch.tensor([sum(spans.values())], device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, spans, clk, ms_with_flush
+
+
+def roofline_of(wl, spans, peaks):
+    """Roofline record of the workload's dominant kernel: algorithmic work per step
+    over its CUDA-event time per step, against the measured peak."""
+    work, bound = wl.work()
+    dom = max(work, key=lambda k: spans.get(k, 0.0))
+    if bound == "tensor":
+        ach = work[dom] / (spans[dom] / 1e3) / 1e12
+        peak, unit, src = peaks["bf16_tflops_sustained"], "TFLOP/s", "sustained bf16"
+    else:
+        ach = work[dom] / (spans[dom] / 1e3) / 1e9
+        peak, unit, src = peaks["hbm_gbs"], "GB/s", "HBM copy"
+    return {"bound": bound, "kernel": dom, "achieved": round(ach, 1), "peak": peak,
+            "unit": unit, "frac": round(ach / peak, 4), "traffic": wl.traffic(dom),
+            "algorithmic_per_step": work[dom],
+            "peak_source": f"{peaks['source']} ({src})",
+            "per_kernel_ms": {k: round(v, 4) for k, v in spans.items()}}
+
+
+# BASELINE.json's per-operator configurations, timed after the headline workload
+PER_OP = ["c1", "c2", "c3", "c4", "c5_sinkhorn"]
+
+
+def per_op_block(rank, world, local, device, barrier, peaks, target_s=0.4):
+    """µs per call, throughput and roofline of each operator at its own
+    configuration (rows split over the ranks like the headline workload).  Each is
+    warmed up, then timed over enough calls to fill ~`target_s` seconds (so the
+    clock sampler sees the region), the same number on every rank."""
+    import torch
+    import torch.distributed as dist
+
+    res = {}
+    for name in PER_OP:
+        wl = WORKLOADS[name](rank, world, device)
+        for _ in range(3):
+            wl.run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            wl.run()
+        e1.record()
+        torch.cuda.synchronize()
+        est = max(e0.elapsed_time(e1) / 3, 1e-3)
+        t = torch.tensor([min(2000, max(10, int(target_s * 1e3 / est)))], device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        steps = int(t.item())
+        ms, spans, clk, ms_flush = timed_region(wl, steps, world, local, device, barrier)
+        rf = roofline_of(wl, spans, peaks)
+        res[name] = {"workload": wl.config()["workload"], "us_per_call": round(ms * 1e3, 2),
+                     "value": wl.units / (ms / 1e3), "unit": wl.metric, "calls": steps,
+                     "launches_per_call": wl.launches_per_step(), "l2": wl.config()["l2"],
+                     "roofline": {k: rf[k] for k in ("bound", "kernel", "achieved", "peak", "unit",
+                                                      "frac", "traffic")},
+                     "clocks": clk}
+        if ms_flush is not None:
+            res[name]["us_per_call_with_l2_flush"] = round(ms_flush * 1e3, 2)
+        del wl
+        torch.cuda.empty_cache()
+    return res
 
 
 def main():
@@ -710,33 +816,7 @@ def main():
             dist.barrier()
 
     # ---- device-resident timed region
-    clocks = ClockSampler(local)
-    clocks.start()
-    timers = Timers()
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(a.steps):
-        wl.run(timers)
-    e1.record()
-    torch.cuda.synchronize()
-    barrier()
-    ms = e0.elapsed_time(e1) / a.steps
-    clk = clocks.stop()
-    ops.device_status()
-    t = torch.tensor([ms], device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    spans = timers.per_step_ms(a.steps)
-    ms_with_flush = None
-    if wl.flushes:
-        ms_with_flush = ms
-        t = torch.tensor([sum(spans.values())], device=device)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms, spans, clk, ms_with_flush = timed_region(wl, a.steps, world, local, device, barrier)
 
     # ---- end to end through the public ops, host buffers
     e2e = None
@@ -748,6 +828,7 @@ def main():
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         wl.e2e_begin()
         for _ in range(a.steps):
@@ -765,19 +846,7 @@ def main():
                "copies": wl.e2e_note()}
 
     peaks = measured_peaks()
-    work, bound = wl.work()
-    dom = max(work, key=lambda k: spans.get(k, 0.0))
-    if bound == "tensor":
-        ach = work[dom] / (spans[dom] / 1e3) / 1e12
-        peak, unit, src = peaks["bf16_tflops_sustained"], "TFLOP/s", "sustained bf16"
-    else:
-        ach = work[dom] / (spans[dom] / 1e3) / 1e9
-        peak, unit, src = peaks["hbm_gbs"], "GB/s", "HBM copy"
-    roofline = {"bound": bound, "kernel": dom, "achieved": round(ach, 1), "peak": peak,
-                "unit": unit, "frac": round(ach / peak, 4), "traffic": wl.traffic(dom),
-                "algorithmic_per_step": work[dom],
-                "peak_source": f"{peaks['source']} ({src})",
-                "per_kernel_ms": {k: round(v, 4) for k, v in spans.items()}}
+    roofline = roofline_of(wl, spans, peaks)
     line = {"metric": wl.metric, "value": wl.units / (ms / 1e3), "unit": wl.metric, "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype,
@@ -791,6 +860,10 @@ def main():
         v, sample = wl.cpu_sample()
         line["cpu_baseline"] = {"value": v, "unit": wl.metric, "cores": os.cpu_count(),
                                 "kind": "port", "sample": sample}
+    if a.workload == "dsa_e2e" and a.tokens is None and not a.no_per_op:
+        del wl
+        torch.cuda.empty_cache()
+        line["per_op"] = per_op_block(rank, world, local, device, barrier, peaks)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -57,11 +57,13 @@ int ks_sinkhorn(const float* x, float* out, int64_t n_mats, int32_t n, int32_t r
  * Top-k sparse attention with a per-head sink logit, baseline/sparse_attention.py:5-42.
  *   q    bf16 [B, M, H, D]     kv bf16 [B, N, D] (shared by all heads: MQA / MLA latent)
  *   sink fp32 [H]              topk_idxs int32 [B, M, K]; entries < 0 are ignored,
- *                              repeated entries count once per occurrence
+ *                              repeated entries count once per occurrence; entries
+ *                              >= N are ignored too and reported as a bounds error
+ *                              by ks_device_status (the reference's gather raises)
  *   out  bf16 [B, M, H, dv]  = output columns [dv_begin, dv_begin + dv) of the
  *                              reference (V is kv[..., dv_begin : dv_begin + dv]).
  * Requirements: H <= 128, D % 64 == 0, D <= 576, dv % 64 == 0 (dv may be any
- * multiple of 64 up to 512), dv_begin % 64 == 0, dv_begin + dv <= D, idx < N.
+ * multiple of 64 up to 512), dv_begin % 64 == 0, dv_begin + dv <= D.
  * Replaces sparse_attn_megakernel_basic_torch,
  * optimized/sparse_attention/op_extension/sparse_attn_torch.cpp:96-160.
  */
@@ -117,6 +119,29 @@ int ks_indexer_scores(const void* q, const void* k, int64_t k_batch_rows, const 
 int ks_topk_rows(const void* scores, int64_t score_ld, int64_t B, int64_t S, int64_t T,
                  int64_t pos0, int32_t causal, int32_t ratio, int32_t topk, int64_t offset,
                  void* out, int32_t out_dtype, void* stream);
+
+/*
+ * One DeepSeek-sparse-attention step over B x S query rows: the indexer
+ * (exactly ks_indexer with out_dtype KS_INT32) selects top-min(topk, T) keys per
+ * row, and sparse attention (exactly ks_sparse_attn with dv_begin = 0 and
+ * K = min(topk, T)) attends to them.  The int32 indices go from the first stage
+ * to the second in idx_out [B, S, min(topk, T)] (also a result), never as int64.
+ *   q_ix, k_ix, w, freqs, rope_dim, pos0, causal, ratio, offset: as ks_indexer
+ *   q_sa bf16 [B, S, H_sa, D_sa], kv bf16 [B, N, D_sa], attn_sink fp32 [H_sa]
+ *   out  bf16 [B, S, H_sa, dv]
+ * The indexer's output (index + offset, or -1) must address rows of kv: entries
+ * >= N are skipped and reported by ks_device_status.  workspace >=
+ * ks_indexer_workspace_size(B, S, T), 256-byte aligned.  T >= 1.
+ * Composes baseline/indexer.py:195-205 (int64 indices) feeding
+ * baseline/sparse_attention.py:16-17 (topk_idxs); the reference has no single
+ * host op for the pair.
+ */
+int ks_dsa(const void* q_ix, const void* k_ix, int64_t k_batch_rows, const void* w,
+           const float* freqs, int64_t B, int64_t S, int64_t H_ix, int64_t D_ix, int64_t T,
+           int32_t rope_dim, int64_t pos0, int32_t causal, int32_t ratio, int32_t topk,
+           int64_t offset, const void* q_sa, const void* kv, int64_t N, const float* attn_sink,
+           int64_t H_sa, int64_t D_sa, int64_t dv, float softmax_scale, int32_t* idx_out,
+           void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * ks_indexer without a workspace argument, for callers that cannot allocate

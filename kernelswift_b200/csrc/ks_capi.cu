@@ -44,6 +44,10 @@ struct Device {
   bool ready = false;
   int* status = nullptr;  // address of g_status_word on this device
   int num_sms = 0;
+  // kernels whose dynamic shared-memory opt-in has been set on this device
+  // (cudaFuncSetAttribute acts on the current device's context only)
+  const void* smem_optin[16] = {};
+  int n_smem_optin = 0;
 };
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
@@ -64,6 +68,20 @@ int device(Device** out) {
     d.ready = true;
   }
   *out = &d;
+  return KS_OK;
+}
+
+// Allow `func` the 227 KB shared-memory maximum on the device `d` describes (the
+// current device), once per device and kernel.
+int smem_optin(Device* d, const void* func, const char* what) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (int i = 0; i < d->n_smem_optin; ++i)
+    if (d->smem_optin[i] == func) return KS_OK;
+  cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  if (d->n_smem_optin >= (int)(sizeof(d->smem_optin) / sizeof(d->smem_optin[0])))
+    return fail(KS_ERR_UNSUPPORTED, "too many kernels with a shared-memory opt-in");
+  d->smem_optin[d->n_smem_optin++] = func;
   return KS_OK;
 }
 
@@ -160,15 +178,12 @@ int indexer_check(const void* q, const void* k, const void* w, const float* freq
 }
 
 template <int H>
-int launch_indexer_scores(const CUtensorMap& qm, const CUtensorMap& km, const IndexerScoreParams& p,
-                          const IndexerGeom& g, int grid, cudaStream_t st) {
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(indexer_score_kernel<H>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
-  });
-  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(indexer)");
+int launch_indexer_scores(Device* dev, const CUtensorMap& qm, const CUtensorMap& km,
+                          const IndexerScoreParams& p, const IndexerGeom& g, int grid,
+                          cudaStream_t st) {
+  if (int rc = smem_optin(dev, reinterpret_cast<const void*>(indexer_score_kernel<H>),
+                          "cudaFuncSetAttribute(indexer)"))
+    return rc;
   indexer_score_kernel<H><<<grid, IX_THREADS, g.smem, st>>>(qm, km, p);
   return launch_check("indexer_score_kernel launch");
 }
@@ -202,20 +217,17 @@ int indexer_scores_impl(const void* q, const void* k, int64_t k_batch_rows, cons
   p.budget_ns = wait_budget_ns();
   const int grid = g.n_items < dev->num_sms ? g.n_items : dev->num_sms;
   switch (H) {
-    case 16: return launch_indexer_scores<16>(qm, km, p, g, grid, st);
-    case 32: return launch_indexer_scores<32>(qm, km, p, g, grid, st);
-    default: return launch_indexer_scores<64>(qm, km, p, g, grid, st);
+    case 16: return launch_indexer_scores<16>(dev, qm, km, p, g, grid, st);
+    case 32: return launch_indexer_scores<32>(dev, qm, km, p, g, grid, st);
+    default: return launch_indexer_scores<64>(dev, qm, km, p, g, grid, st);
   }
 }
 
 template <int EPT>
-int launch_topk(const TopkParams& p, int64_t rows, size_t smem, cudaStream_t st) {
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(topk_rows_kernel<EPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
-  });
-  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(topk)");
+int launch_topk(Device* dev, const TopkParams& p, int64_t rows, size_t smem, cudaStream_t st) {
+  if (int rc = smem_optin(dev, reinterpret_cast<const void*>(topk_rows_kernel<EPT>),
+                          "cudaFuncSetAttribute(topk)"))
+    return rc;
   topk_rows_kernel<EPT><<<(unsigned)rows, TK_THREADS, smem, st>>>(p);
   return launch_check("topk_rows_kernel launch");
 }
@@ -259,10 +271,10 @@ int topk_impl(const void* scores, int64_t score_ld, int64_t B, int64_t S, int64_
   const size_t nbuf = (size_t)TK_THREADS * ept > (size_t)TK_HBINS ? (size_t)TK_THREADS * ept : (size_t)TK_HBINS;
   const size_t smem = nbuf * 4 + (TK_WARPS + 4 + 8 + 2 * TK_WARPS) * 4 + round_up(T, 8) * 2;
   switch (ept) {
-    case 1: return launch_topk<1>(p, B * S, smem, st);
-    case 2: return launch_topk<2>(p, B * S, smem, st);
-    case 4: return launch_topk<4>(p, B * S, smem, st);
-    default: return launch_topk<8>(p, B * S, smem, st);
+    case 1: return launch_topk<1>(dev, p, B * S, smem, st);
+    case 2: return launch_topk<2>(dev, p, B * S, smem, st);
+    case 4: return launch_topk<4>(dev, p, B * S, smem, st);
+    default: return launch_topk<8>(dev, p, B * S, smem, st);
   }
 }
 
@@ -327,12 +339,9 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
   p.budget_ns = wait_budget_ns();
   CUtensorMap qm;
   if (int rc = make_map_bf16(&qm, q, D, (uint64_t)(B * M * H), D * 2, 64, 64)) return rc;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
-  });
-  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute(sparse_attn)");
+  if (int rc = smem_optin(dev, reinterpret_cast<const void*>(sparse_attn_kernel),
+                          "cudaFuncSetAttribute(sparse_attn)"))
+    return rc;
   sparse_attn_kernel<<<(unsigned)(2 * B * M), SA_THREADS, smem, st>>>(qm, p);
   return launch_check("sparse_attn_kernel launch");
 }
@@ -392,7 +401,7 @@ extern "C" {
 
 const char* ks_last_error(void) { return t_err.c_str(); }
 
-int ks_version(void) { return 100; }
+int ks_version(void) { return 101; }
 
 int ks_sinkhorn(const float* x, float* out, int64_t n_mats, int32_t n, int32_t repeat, float eps,
                 void* stream) {
@@ -427,10 +436,9 @@ int ks_sinkhorn(const float* x, float* out, int64_t n_mats, int32_t n, int32_t r
     case 7: launch_reg(sinkhorn_reg_kernel<7>, 7); break;
     case 8: launch_pair(sinkhorn_pair_kernel<8>, 8); break;
     default: {
-      static std::once_flag once;
-      std::call_once(once, [] {
-        cudaFuncSetAttribute(sinkhorn_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
-      });
+      if (int rc = smem_optin(dev, reinterpret_cast<const void*>(sinkhorn_warp_kernel),
+                              "cudaFuncSetAttribute(sinkhorn)"))
+        return rc;
       const size_t smem = (size_t)SKW_WARPS * n * (n + 1) * 4;
       const int64_t blocks = (n_mats + SKW_WARPS - 1) / SKW_WARPS;
       sinkhorn_warp_kernel<<<(unsigned)blocks, SKW_WARPS * 32, smem, st>>>(x, out, n_mats, n, repeat, eps);
@@ -491,6 +499,34 @@ int ks_sparse_attn(const void* q, const void* kv, const float* attn_sink,
                           softmax_scale, static_cast<cudaStream_t>(stream));
 }
 
+int ks_dsa(const void* q_ix, const void* k_ix, int64_t k_batch_rows, const void* w,
+           const float* freqs, int64_t B, int64_t S, int64_t H_ix, int64_t D_ix, int64_t T,
+           int32_t rope_dim, int64_t pos0, int32_t causal, int32_t ratio, int32_t topk,
+           int64_t offset, const void* q_sa, const void* kv, int64_t N, const float* attn_sink,
+           int64_t H_sa, int64_t D_sa, int64_t dv, float softmax_scale, int32_t* idx_out,
+           void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = indexer_check(q_ix, k_ix, w, freqs, B, S, H_ix, D_ix, T, rope_dim, ratio, k_batch_rows))
+    return rc;
+  if (topk < 1 || topk > 4096) return fail(KS_ERR_UNSUPPORTED, "dsa: topk=%d (1..4096)", topk);
+  if (!idx_out || !out) return fail(KS_ERR_INVALID, "dsa: idx_out and out must be set");
+  if (T < 1) return fail(KS_ERR_INVALID, "dsa: T=%lld leaves no key to attend to", (long long)T);
+  const size_t need = ks_indexer_workspace_size(B, S, T);
+  if (!workspace || workspace_bytes < need)
+    return fail(KS_ERR_WORKSPACE, "dsa: workspace of %zu bytes needed", need);
+  if (!aligned(workspace, 256)) return fail(KS_ERR_ALIGNMENT, "dsa: workspace must be 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t ld = round_up(T, 8);
+  const int64_t K = topk < T ? topk : T;
+  if (int rc = indexer_scores_impl(q_ix, k_ix, k_batch_rows, w, freqs, B, S, H_ix, D_ix, T,
+                                   rope_dim, pos0, causal, ratio, workspace, ld, st))
+    return rc;
+  if (int rc = topk_impl(workspace, ld, B, S, T, pos0, causal, ratio, topk, offset, idx_out,
+                         KS_INT32, st))
+    return rc;
+  return sparse_attn_impl(q_sa, kv, attn_sink, idx_out, out, B, S, H_sa, D_sa, N, K, 0, dv,
+                          softmax_scale, st);
+}
+
 int ks_device_status(void* stream) {
   Device* dev;
   if (int rc = device(&dev)) return rc;
@@ -508,7 +544,12 @@ int ks_device_status(void* stream) {
                   "device status %d (a bounded wait timed out: block %d, thread %d, barrier at "
                   "shared offset %d, parity %d, tag %d)",
                   v[0], v[1], (int)((unsigned)v[2] >> 20), (v[2] >> 1) & 0x7FFFF, v[2] & 1, v[3]);
-    return fail(KS_ERR_DEVICE, "device status %d (bounds check failed)", v[0]);
+    if (v[0] == DEV_BOUNDS)
+      return fail(KS_ERR_DEVICE,
+                  "device status %d (query row %d held an index >= its table size %d; the "
+                  "access was skipped)",
+                  v[0], v[1], v[3]);
+    return fail(KS_ERR_DEVICE, "device status %d", v[0]);
   }
   return KS_OK;
 }

@@ -140,6 +140,18 @@ __device__ __forceinline__ void raise_timeout(const WaitCtx& w, uint32_t bar, ui
   }
 }
 
+// An index outside its table was found; the access it named was skipped.  Records
+// DEV_BOUNDS (first error only) with status[1] = `where` (e.g. the query row) and
+// status[3] = `value` (e.g. the table size the index reached).  Unlike a timeout it
+// does not abort the CTA.
+__device__ __forceinline__ void report_bounds(int* status, int where, int value) {
+  if (status && atomicCAS(status, 0, DEV_BOUNDS) == 0) {
+    status[1] = where;
+    status[2] = 0;
+    status[3] = value;
+  }
+}
+
 // Wait until the phase with `parity` of `bar` completes.  Returns false when the
 // CTA is aborting (unless `drain`) or the budget ran out (then the error is
 // recorded).  `drain` waits are the ones that make sure copies and MMAs already

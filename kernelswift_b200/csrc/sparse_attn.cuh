@@ -434,9 +434,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
     float m_used = sink2, lsum = 0.f;
     const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
     const int o_cols = p.dv_pad / 2;
-    // validity bits of this lane's 128 keys of block j (warp-uniform loads)
+    bool oob = false;  // an index >= N was seen (reported once, after the last block)
+    // validity bits of this lane's 128 keys of block j (warp-uniform loads).  An
+    // index >= N (which the reference's gather rejects) is masked like -1 and, in
+    // CTA 0, reported as a bounds error; negative indices are masked silently.
     auto valid_bits = [&](int j, uint32_t* mk) {
       const int k0 = j * SA_NB + half * SA_HALF;
+      // (0 <= v < N as one unsigned compare; v >= N as the OR of the signed ones)
+      const uint32_t un = (uint32_t)p.N;
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
         uint32_t bits = 0;
@@ -446,16 +451,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             const int4 v = __ldg(v4 + q);
-            bits |= (uint32_t)(v.x >= 0 && v.x < p.N) << (4 * q);
-            bits |= (uint32_t)(v.y >= 0 && v.y < p.N) << (4 * q + 1);
-            bits |= (uint32_t)(v.z >= 0 && v.z < p.N) << (4 * q + 2);
-            bits |= (uint32_t)(v.w >= 0 && v.w < p.N) << (4 * q + 3);
+            bits |= (uint32_t)((uint32_t)v.x < un) << (4 * q);
+            bits |= (uint32_t)((uint32_t)v.y < un) << (4 * q + 1);
+            bits |= (uint32_t)((uint32_t)v.z < un) << (4 * q + 2);
+            bits |= (uint32_t)((uint32_t)v.w < un) << (4 * q + 3);
+            oob |= (v.x >= p.N) | (v.y >= p.N) | (v.z >= p.N) | (v.w >= p.N);
           }
         } else {
           for (int i = 0; i < 32; ++i) {
             const int k = kw + i;
             const int32_t v = k < p.K ? __ldg(ip + k) : -1;
-            bits |= (uint32_t)(v >= 0 && v < p.N) << i;
+            bits |= (uint32_t)((uint32_t)v < un) << i;
+            oob |= v >= p.N;
           }
         }
         mk[w] = bits;
@@ -576,6 +583,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       }
       if (lane == 0) KS_SA_TRACE(11, 16 * q4 + j);
     }
+    if (cta == 0 && __any_sync(0xFFFFFFFFu, oob) && oob) report_bounds(p.status, (int)token, p.N);
     if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->o_full, 0, wc));
     // tail: the last two "P free" signals land before the CTA exits (see the gathers)
     for (int jj = p.nblk - 2; ok && jj < p.nblk; ++jj)

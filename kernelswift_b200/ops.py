@@ -8,6 +8,7 @@ These are the B200 counterparts of the reference's torch extension ops
 * ``indexer_topk``    <- ``indexer_ops.rope_inplace`` + ``fused_qk_reduce`` + ``topk_mask``
   (indexer_torch.cpp:100-268), fused behind one call
 * ``indexer_scores`` / ``topk_rows`` expose the two indexer stages separately.
+* ``dsa`` runs the indexer's int32 top-k straight into ``sparse_attn`` in one call.
 
 Every op runs on the current CUDA stream of its input's device, validates its
 arguments like the reference (a ``RuntimeError`` on a bad dtype, device, shape
@@ -33,6 +34,33 @@ def _require_cuda(name: str, *tensors: torch.Tensor) -> None:
         raise RuntimeError(f"{name}: inputs must be on one device")
 
 
+def _check_out(name: str, out: torch.Tensor, shape, dtype, device) -> None:
+    """A caller-supplied output must be exactly what the kernel writes: the kernels
+    take a raw pointer and would write past a smaller or differently typed buffer."""
+    if not isinstance(out, torch.Tensor):
+        raise RuntimeError(f"{name}: out must be a tensor")
+    if out.dtype != dtype:
+        raise RuntimeError(f"{name}: out must be {dtype}, got {out.dtype}")
+    if tuple(out.shape) != tuple(shape):
+        raise RuntimeError(f"{name}: out must have shape {tuple(shape)}, got {tuple(out.shape)}")
+    if out.device != device:
+        raise RuntimeError(f"{name}: out must be on {device}, got {out.device}")
+    if not out.is_contiguous():
+        raise RuntimeError(f"{name}: out must be contiguous")
+
+
+def _check_workspace(name: str, ws: torch.Tensor, need: int, device) -> None:
+    if not isinstance(ws, torch.Tensor):
+        raise RuntimeError(f"{name}: workspace must be a tensor")
+    if ws.device != device:
+        raise RuntimeError(f"{name}: workspace must be on {device}, got {ws.device}")
+    if not ws.is_contiguous():
+        raise RuntimeError(f"{name}: workspace must be contiguous")
+    if ws.numel() * ws.element_size() < need:
+        raise RuntimeError(f"{name}: workspace of {need} bytes needed, got "
+                           f"{ws.numel() * ws.element_size()}")
+
+
 def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
@@ -49,7 +77,10 @@ def sinkhorn(x: torch.Tensor, repeat: int = 10, eps: float = 1e-6,
     if x.dim() < 2 or x.shape[-1] != x.shape[-2]:
         raise RuntimeError("sinkhorn: x must be [..., n, n]")
     _require_cuda("sinkhorn", x)
-    out = torch.empty_like(x) if out is None else out
+    if out is None:
+        out = torch.empty_like(x)
+    else:
+        _check_out("sinkhorn", out, x.shape, torch.float32, x.device)
     n = x.shape[-1]
     n_mats = x.numel() // (n * n) if n else 0
     with torch.cuda.device(x.device):
@@ -85,6 +116,8 @@ def sparse_attn(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor,
     dv = D if dv is None else int(dv)
     if out is None:
         out = torch.empty((B, M, H, dv), dtype=torch.bfloat16, device=q.device)
+    else:
+        _check_out("sparse_attn", out, (B, M, H, dv), torch.bfloat16, q.device)
     with torch.cuda.device(q.device):
         if dv <= _DV_MAX:
             check(lib().ks_sparse_attn(_ptr(q), _ptr(kv), _ptr(attn_sink), _ptr(topk_idxs),
@@ -135,18 +168,81 @@ def indexer_topk(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, freqs: torch
     kk = min(int(topk), int(T))
     if out is None:
         out = torch.empty((B, S, kk), dtype=out_dtype, device=q.device)
+    elif out.dtype not in (torch.int32, torch.int64):
+        raise RuntimeError("indexer: out must be int32 or int64")
+    else:
+        _check_out("indexer", out, (B, S, kk), out.dtype, q.device)
     if T == 0:
         return out
     need = indexer_workspace_size(B, S, T)
-    if workspace is None or workspace.numel() < need:
+    if workspace is None:
         workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    else:
+        _check_workspace("indexer", workspace, need, q.device)
     with torch.cuda.device(q.device):
         check(lib().ks_indexer(_ptr(q), _ptr(k), k.shape[1], _ptr(w), _ptr(freqs), B, S, H, D,
                                int(T), int(rope_dim), int(pos0), int(bool(causal)), int(ratio),
                                int(topk), int(offset), _ptr(out),
                                KS_INT64 if out.dtype == torch.int64 else KS_INT32,
-                               _ptr(workspace), workspace.numel(), _stream(q)), "ks_indexer")
+                               _ptr(workspace), workspace.numel() * workspace.element_size(),
+                               _stream(q)), "ks_indexer")
     return out
+
+
+def dsa(q_ix: torch.Tensor, k_ix: torch.Tensor, w: torch.Tensor, freqs: torch.Tensor | None,
+        rope_dim: int, T: int, topk: int, q_sa: torch.Tensor, kv: torch.Tensor,
+        attn_sink: torch.Tensor, softmax_scale: float, dv: int | None = None, ratio: int = 1,
+        causal: bool = True, offset: int = 0, pos0: int = 0, out: torch.Tensor | None = None,
+        idx_out: torch.Tensor | None = None, workspace: torch.Tensor | None = None
+        ) -> tuple[torch.Tensor, torch.Tensor]:
+    """One DeepSeek-sparse-attention step in a single library call: the indexer's
+    top-k (``indexer_topk`` with int32 output) feeding ``sparse_attn`` on the same
+    query rows (baseline/indexer.py:195-205 -> baseline/sparse_attention.py:16-17).
+
+    q_ix bf16 [B,S,H_ix,D_ix] before RoPE, k_ix bf16 [B,Tk>=T,D_ix], w bf16
+    [B,S,H_ix], freqs fp32 [S, rope_dim/2, 2]; q_sa bf16 [B,S,H_sa,D_sa], kv bf16
+    [B,N,D_sa], attn_sink fp32 [H_sa].  Returns (out bf16 [B,S,H_sa,dv], indices
+    int32 [B,S,min(topk,T)])."""
+    B, S, H, D = _indexer_args(q_ix, k_ix, w, freqs, T)
+    if q_sa.dtype != torch.bfloat16 or kv.dtype != torch.bfloat16:
+        raise RuntimeError("dsa: q_sa and kv must be bfloat16")
+    if attn_sink.dtype != torch.float32:
+        raise RuntimeError("dsa: attn_sink must be float32")
+    if q_sa.dim() != 4 or kv.dim() != 3 or attn_sink.dim() != 1:
+        raise RuntimeError("dsa: expected q_sa [b,s,h,d], kv [b,n,d], attn_sink [h]")
+    if q_sa.shape[0] != B or q_sa.shape[1] != S:
+        raise RuntimeError("dsa: q_sa must have the indexer's [b, s] rows")
+    H_sa, D_sa = q_sa.shape[2], q_sa.shape[3]
+    if kv.shape[0] != B or kv.shape[2] != D_sa or attn_sink.shape[0] != H_sa:
+        raise RuntimeError("dsa: kv / attn_sink shape mismatch")
+    _require_cuda("dsa", q_ix, q_sa, kv, attn_sink)
+    if int(T) < 1:
+        raise RuntimeError("dsa: T must be >= 1")
+    dv = D_sa if dv is None else int(dv)
+    if dv > _DV_MAX:
+        raise RuntimeError(f"dsa: dv={dv} > {_DV_MAX} (use indexer_topk + sparse_attn)")
+    kk = min(int(topk), int(T))
+    if idx_out is None:
+        idx_out = torch.empty((B, S, kk), dtype=torch.int32, device=q_ix.device)
+    else:
+        _check_out("dsa", idx_out, (B, S, kk), torch.int32, q_ix.device)
+    if out is None:
+        out = torch.empty((B, S, H_sa, dv), dtype=torch.bfloat16, device=q_ix.device)
+    else:
+        _check_out("dsa", out, (B, S, H_sa, dv), torch.bfloat16, q_ix.device)
+    need = indexer_workspace_size(B, S, T)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q_ix.device)
+    else:
+        _check_workspace("dsa", workspace, need, q_ix.device)
+    with torch.cuda.device(q_ix.device):
+        check(lib().ks_dsa(_ptr(q_ix), _ptr(k_ix), k_ix.shape[1], _ptr(w), _ptr(freqs), B, S, H, D,
+                           int(T), int(rope_dim), int(pos0), int(bool(causal)), int(ratio),
+                           int(topk), int(offset), _ptr(q_sa), _ptr(kv), kv.shape[1],
+                           _ptr(attn_sink), H_sa, D_sa, dv, float(softmax_scale), _ptr(idx_out),
+                           _ptr(out), _ptr(workspace), workspace.numel() * workspace.element_size(),
+                           _stream(q_ix)), "ks_dsa")
+    return out, idx_out
 
 
 def indexer_scores(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, freqs: torch.Tensor | None,

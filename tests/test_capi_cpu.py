@@ -16,7 +16,7 @@ def header_functions():
 def test_header_declares_the_operators():
     names = header_functions()
     for n in ("ks_sinkhorn", "ks_sparse_attn", "ks_indexer", "ks_indexer_scores", "ks_topk_rows",
-              "ks_indexer_workspace_size", "ks_last_error", "ks_device_status"):
+              "ks_indexer_workspace_size", "ks_dsa", "ks_last_error", "ks_device_status"):
         assert n in names
 
 
@@ -31,7 +31,7 @@ def test_python_signatures_cover_header(built_lib):
 
     assert sorted(_lib.SIGNATURES) == header_functions()
     lib = _lib.lib()
-    assert lib.ks_version() == 100
+    assert lib.ks_version() == 101
     assert lib.ks_last_error() == b""
 
 

@@ -76,6 +76,20 @@ def test_golden(cuda_ok, name):
     valid = np.broadcast_to(np.arange(T)[None, None, :] < lim[None, :, None], sc.shape)
     assert ((sc == d["scores"]) | ~valid).mean() > 0.999
     assert idx.shape == d["out"].shape and np.array_equal(idx < 0, d["out"] < 0)
+    # The kernel's indices against the reference's own torch.topk output, read as
+    # sequences of the reference's score values: torch's CPU tie order is
+    # unspecified, so equal values may come in another index order, but the value
+    # sequence must match, except in rows where the kernel's scores carry a flip.
+    ref_sc = np.where(valid, d["scores"], O.NEG_INF_BF16)
+    key = O.bf16_order_key(ref_sc).astype(np.int64)
+
+    def values(ix):
+        raw = np.where(ix < 0, 0, ix - off)
+        return np.where(ix < 0, -1, np.take_along_axis(key, raw, axis=-1))
+
+    differ = np.any(values(idx) != values(d["out"]), axis=-1)
+    flipped = np.any((sc != d["scores"]) & valid, axis=-1)
+    assert not np.any(differ & ~flipped), "index value sequences differ in rows without a flip"
 
 
 GEOMS = [

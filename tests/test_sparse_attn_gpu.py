@@ -171,3 +171,28 @@ def test_repeatable(cuda_ok, B, M, H, D, N, K, dv, mode):
         assert torch.equal(outs[0], o)
     ref = O.sparse_attn(bits_from_bf16(q), bits_from_bf16(kv), s.cpu().numpy(), idx.cpu().numpy(), D ** -0.5, dv)
     assert_close(bits_from_bf16(outs[0]), ref)
+
+
+def test_out_of_range_index_reported(cuda_ok):
+    """An index >= N (the reference's gather raises on it,
+    baseline/sparse_attention.py:19-21) is skipped like -1 and reported as a bounds
+    error by the status check, without faulting; the status is cleared once read."""
+    from kernelswift_b200 import _lib, ops
+
+    B, M, H, D, N, K = 1, 3, 16, 128, 200, 64
+    q, kv, s, idx = make_case(B, M, H, D, N, K, seed=31)
+    bad = idx.clone()
+    bad[0, 1, 5] = N          # just past the table
+    bad[0, 2, 0] = N + 12345  # far past it
+    out = ops.sparse_attn(q.cuda(), kv.cuda(), s.cuda(), bad.cuda(), D ** -0.5)
+    with pytest.raises(_lib.KsError) as e:
+        ops.device_status()
+    assert e.value.code == _lib.KS_ERR_DEVICE and "table size" in str(e.value)
+    ops.device_status()  # cleared
+    masked = bad.clone()
+    masked[masked >= N] = -1
+    ref = O.sparse_attn(bits_from_bf16(q), bits_from_bf16(kv), s.numpy(), masked.numpy(), D ** -0.5)
+    assert_close(bits_from_bf16(out), ref)
+    # in-range calls leave the status clean
+    ops.sparse_attn(q.cuda(), kv.cuda(), s.cuda(), idx.cuda(), D ** -0.5)
+    ops.device_status()
