@@ -164,6 +164,46 @@ def indexer_cases(ref):
     run("ix_ties", 1, 128, 64, 16, 64, 32, 32, 64, 1, 0, 7, 14, ties=True)
 
 
+def harness_cases(ref, seed=42):
+    """Each reference Model at its own default configuration, built and run in the
+    order the reference harness uses (benchmarks/ks/auto_bench.py:378-409 and
+    :513-539): seed, get_init_inputs (twice, v0 then v1), Model(*init), seed,
+    get_inputs, seed, forward on a clone of the inputs.  Outputs that are too large
+    to store whole are kept as sampled rows plus per-row sums."""
+
+    def seed_all():
+        torch.manual_seed(seed)
+
+    for rel, name in (("baseline/sinkhorn.py", "sinkhorn"),
+                      ("baseline/sparse_attention.py", "sparse_attention"),
+                      ("baseline/indexer.py", "indexer")):
+        m = load(ref, rel, "ref_h_" + name)
+        seed_all()
+        m.get_init_inputs()
+        seed_all()
+        init = m.get_init_inputs()
+        model = m.Model(*init)
+        model.eval()
+        seed_all()
+        inputs = m.get_inputs()
+        seed_all()
+        cloned = [t.clone() if isinstance(t, torch.Tensor) else t for t in inputs]
+        with torch.no_grad():
+            out = model(*cloned)
+        path = os.path.join(HERE, "hx_" + name + ".npz")
+        if name == "sinkhorn":
+            np.savez_compressed(path, out=out.numpy())
+        elif name == "sparse_attention":
+            B, M = out.shape[:2]
+            rows = np.array([0, 1, M // 2, M - 1])
+            np.savez_compressed(path, rows=rows, out_rows=bits(out[:, rows]),
+                                row_sums=out.double().sum(dim=(2, 3)).numpy())
+        else:
+            assert out.dtype == torch.int64 and int(out.max()) < 32768
+            np.savez_compressed(path, out=out.numpy().astype(np.int16))
+        print("hx_" + name, tuple(out.shape), out.dtype)
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path to a KernelSwift checkout")
@@ -172,3 +212,4 @@ if __name__ == "__main__":
     sinkhorn_cases(a.ref)
     sparse_attn_cases(a.ref)
     indexer_cases(a.ref)
+    harness_cases(a.ref)
