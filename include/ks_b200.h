@@ -144,6 +144,44 @@ int ks_dsa(const void* q_ix, const void* k_ix, int64_t k_batch_rows, const void*
            void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * e4m3 (fp8) quantisation of bf16 rows [rows, D] with one power-of-two scale
+ * per row (the "ue8m0" scale format of ModelArgs, baseline/indexer.py:15):
+ * scale[r] = the smallest power of two >= max(max_i |x[r,i]|, 1e-4) / 448 and
+ * x8[r,i] = e4m3(x[r,i] / scale[r]) rounded to nearest even, saturating at +-448.
+ * D % 4 == 0; x 8-byte aligned, x8 and scale 4-byte aligned.  Prepares the
+ * queries (per token and head) and keys (per key) of ks_indexer_fp8.
+ * The reference declares the FP8 option but implements no kernel for it.
+ */
+int ks_quant_fp8_rows(const void* x, void* x8, float* scale, int64_t rows, int32_t D,
+                      void* stream);
+
+/*
+ * FP8 lightning indexer: ks_indexer with e4m3 queries and keys (ModelArgs.dtype
+ * = "fp8", baseline/indexer.py:14; the bf16 baseline declares but does not use
+ * it).  Scores
+ *   bf16( k_scale[b,t] * sum_h( relu(q8[b,s,h,:] . k8[b,t,:]) * w[b,s,h] ) )
+ * with the dot products from the tensor cores (fp32 accumulation), each
+ * product and partial sum in fp32 rounded to nearest in head order; then the
+ * causal mask, top-k and -1/offset post-processing of ks_indexer.
+ *   q8 e4m3 [B, S, H, D] (rotated before quantisation: no RoPE here), D = 128
+ *   k8 e4m3 keys; batch b, key t at k8 + (b * k_batch_rows + t) * D
+ *   w  fp32 [B, S, H]  head weight x the query row's scale (x D^-0.5 H^-0.5)
+ *   k_scale fp32 per key row, laid out like the rows of k8
+ * out, workspace, pos0, causal, ratio, topk, offset: as ks_indexer.
+ */
+int ks_indexer_fp8(const void* q8, const void* k8, int64_t k_batch_rows, const float* w,
+                   const float* k_scale, int64_t B, int64_t S, int64_t H, int64_t D, int64_t T,
+                   int64_t pos0, int32_t causal, int32_t ratio, int32_t topk, int64_t offset,
+                   void* out, int32_t out_dtype, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* Score stage of ks_indexer_fp8 alone (bf16 scores laid out as ks_indexer_scores). */
+int ks_indexer_fp8_scores(const void* q8, const void* k8, int64_t k_batch_rows, const float* w,
+                          const float* k_scale, int64_t B, int64_t S, int64_t H, int64_t D,
+                          int64_t T, int64_t pos0, int32_t causal, int32_t ratio, void* scores,
+                          int64_t score_ld, void* stream);
+
+/*
  * ks_indexer without a workspace argument, for callers that cannot allocate
  * device memory: processes whose device memory belongs to another allocator
  * (a framework's caching allocator or a fixed memory pool that must not be

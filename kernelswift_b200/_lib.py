@@ -47,6 +47,13 @@ SIGNATURES = {
     "ks_dsa": (ctypes.c_int, [_vp, _vp, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                               _c_i32, _c_i64, _c_i32, _c_i32, _c_i32, _c_i64, _vp, _vp, _c_i64, _vp,
                               _c_i64, _c_i64, _c_i64, _c_f32, _vp, _vp, _vp, _sz, _vp]),
+    "ks_quant_fp8_rows": (ctypes.c_int, [_vp, _vp, _vp, _c_i64, _c_i32, _vp]),
+    "ks_indexer_fp8": (ctypes.c_int, [_vp, _vp, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64,
+                                      _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i64, _vp, _c_i32,
+                                      _vp, _sz, _vp]),
+    "ks_indexer_fp8_scores": (ctypes.c_int, [_vp, _vp, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64,
+                                             _c_i64, _c_i64, _c_i64, _c_i32, _c_i32, _vp, _c_i64,
+                                             _vp]),
     "ks_device_status": (ctypes.c_int, [_vp]),
     "ks_selftest_wait_timeout": (ctypes.c_int, [_c_u64, _vp]),
 }

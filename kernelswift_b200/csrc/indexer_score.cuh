@@ -21,7 +21,20 @@
 // Accumulators: 2 x 256 TMEM columns (double buffered), 512 columns in total.
 // Work items (batch, token group) are handed out heaviest-first (causal cost
 // grows with the position), strided over CTAs.
+//
+// FP8 variant (F8 = true; DeepSeek-style FP8 indexer keys and queries, the
+// ModelArgs.dtype = "fp8" / scale_fmt = "ue8m0" option of baseline/indexer.py:14-17,
+// which the bf16 baseline declares but does not use): q and k are e4m3 with one
+// scale per (token, head) row of q and per key row of k; the GEMM runs as
+// tcgen05 kind::f8f6f4 (K = 32 per instruction, 128-byte rows: D = 128 only, no
+// RoPE in the kernel: q is rotated before it is quantised), and the epilogue is
+//   score[b,s,t] = bf16( k_scale[b,t] * sum_h ( relu(q8[b,s,h,:] . k8[b,t,:]) * w[b,s,h] ) )
+// in fp32 (each product and each partial sum rounded to nearest, heads in order),
+// with w fp32 = head weight x the query row's scale.  The bf16 result feeds the
+// same exact top-k as the bf16 path.
 #pragma once
+#include <type_traits>
+
 #include "ks_device.cuh"
 
 namespace ks {
@@ -36,7 +49,9 @@ constexpr int IX_MAX_KST = 8;
 
 struct IndexerScoreParams {
   const float* freqs;  // [S, rd/2, 2] (cos, sin) for the rows' positions
-  const uint16_t* w;   // bf16 [B, S, H] (batch stride w_bs elements)
+  const uint16_t* w;   // bf16 [B, S, H] (batch stride w_bs elements); bf16 path
+  const float* wf;     // fp32 [B, S, H] (batch stride w_bs elements); FP8 path
+  const float* k_scale;  // fp32 per key row, batch b key t at b * k_rows_per_batch + t; FP8 path
   int64_t w_bs;
   int32_t w_vec16;     // w and w_bs allow 16-byte loads
   uint16_t* scores;    // bf16 [B*S, score_ld]
@@ -50,6 +65,7 @@ struct IndexerScoreParams {
   uint64_t budget_ns;
 };
 
+template <bool F8>
 struct IxShared {
   uint64_t k_full[IX_MAX_KST], k_empty[IX_MAX_KST];
   uint64_t acc_full[2], acc_empty[2];
@@ -58,12 +74,18 @@ struct IxShared {
   uint64_t w_full, w_free;  // item weights staged / every epilogue warp done with them
   uint32_t tmem_base;
   int abort;
-  // head weights of the current work item's tokens (token-major, IX_N = tok * H
-  // bf16), staged once per item: read per tile from shared memory rather than
-  // through the global-load path, whose traffic slowed the MMAs
-  alignas(16) uint16_t wbuf[IX_N];
+  // head weights of the current work item's tokens (token-major, IX_N = tok * H;
+  // bf16, or fp32 on the FP8 path), staged once per item: read per tile from
+  // shared memory rather than through the global-load path, whose traffic slowed
+  // the MMAs
+  alignas(16) typename std::conditional<F8, float, uint16_t>::type wbuf[IX_N];
 };
-static_assert(sizeof(IxShared) <= 1024, "IxShared exceeds its 1 KB header");
+// shared-memory header in front of the tiles (the bf16 path keeps 1 KB: one more
+// would cost it a key stage)
+template <bool F8>
+__host__ __device__ constexpr uint32_t ix_hdr_bytes() { return F8 ? 2048u : 1024u; }
+static_assert(sizeof(IxShared<false>) <= ix_hdr_bytes<false>(), "IxShared exceeds its header");
+static_assert(sizeof(IxShared<true>) <= ix_hdr_bytes<true>(), "IxShared exceeds its header");
 
 __device__ __forceinline__ int ix_item_tiles(const IndexerScoreParams& p, int item, int& b,
                                              int& g) {
@@ -80,19 +102,21 @@ __device__ __forceinline__ int ix_item_tiles(const IndexerScoreParams& p, int it
   return (int)((kmax + IX_TILE_KEYS - 1) / IX_TILE_KEYS);
 }
 
-template <int H>
+template <int H, bool F8>
 __global__ void __launch_bounds__(IX_THREADS, 1)
     indexer_score_kernel(const __grid_constant__ CUtensorMap qmap,
                          const __grid_constant__ CUtensorMap kmap, IndexerScoreParams p) {
   extern __shared__ uint8_t ix_raw[];
   const uint32_t raw_addr = smem_u32(ix_raw);
   uint8_t* smem = ix_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  // layout: [IxShared, padded to 1 KB][2 query tiles][kst key stages], 1 KB aligned
+  // layout: [IxShared, padded to its header][2 query tiles][kst key stages], 1 KB aligned
   const int D = p.D;
-  const uint32_t q_bytes = (uint32_t)IX_N * D * 2;         // one query tile
-  const uint32_t k_bytes = (uint32_t)IX_TILE_KEYS * D * 2;  // one key stage
-  IxShared* sh = reinterpret_cast<IxShared*>(smem);
-  uint8_t* qbuf = smem + 1024;
+  constexpr uint32_t ESZ = F8 ? 1 : 2;                        // bytes per element
+  const uint32_t q_bytes = (uint32_t)IX_N * D * ESZ;          // one query tile
+  const uint32_t k_bytes = (uint32_t)IX_TILE_KEYS * D * ESZ;  // one key stage
+  const int nkb = D * (int)ESZ / 128;                         // 128-byte K blocks per row
+  IxShared<F8>* sh = reinterpret_cast<IxShared<F8>*>(smem);
+  uint8_t* qbuf = smem + ix_hdr_bytes<F8>();
   uint8_t* kbuf = qbuf + 2 * q_bytes;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -140,18 +164,18 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
         if (!(ok = mbar_wait(&sh->q_empty[qs], ((qc >> 1) & 1) ^ 1, wc))) break;
         mbar_expect_tx(&sh->q_tma[qs], q_bytes);
         const int32_t qrow = (int32_t)(((int64_t)b * p.S + (int64_t)g * p.tok) * p.H);
-        for (int kb = 0; kb < D / 64; ++kb)
-          tma_load_2d(&qmap, &sh->q_tma[qs], qbuf + qs * q_bytes + kb * (IX_N * 128), kb * 64,
-                      qrow);
+        for (int kb = 0; kb < nkb; ++kb)
+          tma_load_2d(&qmap, &sh->q_tma[qs], qbuf + qs * q_bytes + kb * (IX_N * 128),
+                      kb * (int)(128 / ESZ), qrow);
         ++qc;
         for (int t = 0; t < nt; ++t) {
           const int st = kc % p.kst;
           if (!(ok = mbar_wait(&sh->k_empty[st], ((kc / p.kst) & 1) ^ 1, wc))) break;
           mbar_expect_tx(&sh->k_full[st], k_bytes);
           const int32_t krow = (int32_t)(b * p.k_rows_per_batch + t * IX_TILE_KEYS);
-          for (int kb = 0; kb < D / 64; ++kb)
+          for (int kb = 0; kb < nkb; ++kb)
             tma_load_2d(&kmap, &sh->k_full[st], kbuf + st * k_bytes + kb * (IX_TILE_KEYS * 128),
-                        kb * 64, krow);
+                        kb * (int)(128 / ESZ), krow);
           ++kc;
         }
       }
@@ -164,7 +188,8 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(IX_TILE_KEYS, IX_N, false, false);
+      const uint32_t idesc =
+          F8 ? idesc_e4m3_f32(IX_TILE_KEYS, IX_N) : idesc_bf16_f32(IX_TILE_KEYS, IX_N, false, false);
       uint32_t kc = 0, qc = 0, ac = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
@@ -181,12 +206,16 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
           tc_fence_after();
           const uint32_t kaddr = smem_u32(kbuf + st * k_bytes);
           const uint32_t d_tmem = tmem + as * IX_N;
-          for (int kb = 0; kb < D / 64; ++kb) {
+          // 32 bytes of K per instruction: 16 bf16 or 32 e4m3 elements
+          for (int kb = 0; kb < nkb; ++kb) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t ad = sdesc_sw128(kaddr + kb * (IX_TILE_KEYS * 128) + kk * 32, 16, 1024);
               const uint64_t bd = sdesc_sw128(qaddr + kb * (IX_N * 128) + kk * 32, 16, 1024);
-              umma_bf16_ss(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+              if constexpr (F8)
+                umma_f8_ss(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+              else
+                umma_bf16_ss(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
             }
           }
           umma_commit(&sh->k_empty[st]);
@@ -275,17 +304,32 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
         const int n = lane * 8;  // 8 consecutive weights of token n / H
         const int u = n / H, h0 = n % H;
         const int su = g * TOK + u;
-        const uint16_t* src = p.w + (int64_t)b * p.w_bs + (int64_t)(su < p.S ? su : p.S - 1) * H + h0;
-        uint4 v;
-        if (p.w_vec16) {
-          v = __ldg(reinterpret_cast<const uint4*>(src));
+        const int64_t off = (int64_t)b * p.w_bs + (int64_t)(su < p.S ? su : p.S - 1) * H + h0;
+        if constexpr (F8) {
+          const float* src = p.wf + off;
+          float4 v0, v1;
+          if (p.w_vec16) {
+            v0 = __ldg(reinterpret_cast<const float4*>(src));
+            v1 = __ldg(reinterpret_cast<const float4*>(src) + 1);
+          } else {
+            v0 = make_float4(__ldg(src), __ldg(src + 1), __ldg(src + 2), __ldg(src + 3));
+            v1 = make_float4(__ldg(src + 4), __ldg(src + 5), __ldg(src + 6), __ldg(src + 7));
+          }
+          reinterpret_cast<float4*>(sh->wbuf + n)[0] = v0;
+          reinterpret_cast<float4*>(sh->wbuf + n)[1] = v1;
         } else {
-          uint32_t x[4];
+          const uint16_t* src = p.w + off;
+          uint4 v;
+          if (p.w_vec16) {
+            v = __ldg(reinterpret_cast<const uint4*>(src));
+          } else {
+            uint32_t x[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) x[i] = (uint32_t)__ldg(src + 2 * i) | ((uint32_t)__ldg(src + 2 * i + 1) << 16);
-          v = make_uint4(x[0], x[1], x[2], x[3]);
+            for (int i = 0; i < 4; ++i) x[i] = (uint32_t)__ldg(src + 2 * i) | ((uint32_t)__ldg(src + 2 * i + 1) << 16);
+            v = make_uint4(x[0], x[1], x[2], x[3]);
+          }
+          *reinterpret_cast<uint4*>(sh->wbuf + n) = v;
         }
-        *reinterpret_cast<uint4*>(sh->wbuf + n) = v;
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh->w_full);
       }
@@ -295,6 +339,53 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
         if (!(ok = mbar_wait_inl(&sh->acc_full[as], (ac >> 1) & 1, wc))) break;
         tc_fence_after();
         const int key = t * IX_TILE_KEYS + quarter * 32 + lane;
+        if constexpr (F8) {
+          // per key: k_scale * sum_h relu(dot) * w, products and partial sums rounded
+          // separately, two tokens at a time as one f32x2 pair
+          const float ksc = key < p.T ? __ldg(p.k_scale + (int64_t)b * p.k_rows_per_batch + key) : 0.f;
+#pragma unroll 1
+          for (int jp = 0; jp < TOK_HALF; jp += 2) {
+            const int j0 = half * TOK_HALF + jp;
+            const int s0 = g * TOK + j0, s1 = s0 + 1;
+            const float* wrow0 = sh->wbuf + j0 * H;
+            const float* wrow1 = wrow0 + H;
+            const uint32_t col0 = tmem + as * IX_N + j0 * H + ((uint32_t)(quarter * 32) << 16);
+            uint64_t acc = 0;  // (token s0, token s1) partial sums, f32x2
+#pragma unroll
+            for (int c = 0; c < H; c += 16) {
+              uint32_t r0[16], r1[16];
+              tmem_ld16(col0 + c, r0);
+              tmem_ld16(col0 + H + c, r1);
+              float w0[16], w1[16];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float4 a = reinterpret_cast<const float4*>(wrow0 + c)[i];
+                const float4 bq = reinterpret_cast<const float4*>(wrow1 + c)[i];
+                w0[4 * i] = a.x; w0[4 * i + 1] = a.y; w0[4 * i + 2] = a.z; w0[4 * i + 3] = a.w;
+                w1[4 * i] = bq.x; w1[4 * i + 1] = bq.y; w1[4 * i + 2] = bq.z; w1[4 * i + 3] = bq.w;
+              }
+              tmem_wait_ld();
+#pragma unroll
+              for (int h = 0; h < 16; ++h) {
+                const float a0 = fmaxf(__uint_as_float(r0[h]), 0.f);
+                const float a1 = fmaxf(__uint_as_float(r1[h]), 0.f);
+                asm("{ .reg .b64 x, y, t; mov.b64 x, {%1, %2}; mov.b64 y, {%3, %4};"
+                    " mul.rn.f32x2 t, x, y; add.rn.f32x2 %0, %0, t; }"
+                    : "+l"(acc) : "f"(a0), "f"(a1), "f"(w0[h]), "f"(w1[h]));
+              }
+            }
+            float acc0, acc1;
+            asm("mov.b64 {%0, %1}, %2;" : "=f"(acc0), "=f"(acc1) : "l"(acc));
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int s = u ? s1 : s0;
+              uint16_t out = __bfloat16_as_ushort(__float2bfloat16_rn(__fmul_rn(u ? acc1 : acc0, ksc)));
+              if (key >= lims[jp + u]) out = 0xFF80;  // -inf
+              if (s < p.S && key < p.T)
+                p.scores[((int64_t)b * p.S + s) * p.score_ld + key] = out;
+            }
+          }
+        } else {
 #pragma unroll 1
         for (int jp = 0; jp < TOK_HALF; jp += 2) {
           const int j0 = half * TOK_HALF + jp;
@@ -343,6 +434,7 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
               p.scores[((int64_t)b * p.S + s) * p.score_ld + key] = out;
           }
         }
+        }  // bf16 path
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh->acc_empty[as]);

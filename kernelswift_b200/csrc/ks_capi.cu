@@ -12,6 +12,7 @@
 #include "ks_b200.h"
 #include "ks_device.cuh"
 #include "indexer_score.cuh"
+#include "quant_fp8.cuh"
 #include "sinkhorn.cuh"
 #include "sparse_attn.cuh"
 #include "topk.cuh"
@@ -134,6 +135,23 @@ int make_map_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t row
   return KS_OK;
 }
 
+// 8-bit 2D tensor map [rows, inner] (e4m3 bytes), 128-byte swizzle, box
+// (box_inner x box_rows).
+int make_map_u8(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
+                uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(KS_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                  es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return KS_OK;
+}
+
 int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 
 // ------------------------------------------------------------------ indexer helpers
@@ -142,16 +160,17 @@ struct IndexerGeom {
   size_t smem;
 };
 
-int indexer_geom(int64_t B, int64_t S, int64_t H, int64_t D, IndexerGeom* g) {
+int indexer_geom(int64_t B, int64_t S, int64_t H, int64_t D, bool f8, IndexerGeom* g) {
   g->tok = (int)(IX_N / H);
   g->n_groups = (int)((S + g->tok - 1) / g->tok);
   g->n_items = (int)(B * g->n_groups);
-  const size_t q_bytes = (size_t)IX_N * D * 2, k_bytes = (size_t)IX_TILE_KEYS * D * 2;
+  const size_t esz = f8 ? 1 : 2;
+  const size_t q_bytes = (size_t)IX_N * D * esz, k_bytes = (size_t)IX_TILE_KEYS * D * esz;
   const size_t fixed = 1024 /* alignment slack */ + 2 * q_bytes;
   const size_t limit = 232448;  // 227 KB opt-in maximum per CTA on sm_100
-  const size_t hdr = 1024;      // IxShared, padded
+  const size_t hdr = f8 ? ix_hdr_bytes<true>() : ix_hdr_bytes<false>();  // IxShared, padded
   int kst = (int)((limit - fixed - hdr) / k_bytes);
-  if (kst > 4) kst = 4;
+  if (kst > (f8 ? 8 : 4)) kst = f8 ? 8 : 4;
   if (kst < 2) return fail(KS_ERR_UNSUPPORTED, "indexer: D=%lld leaves no room for key stages", (long long)D);
   g->kst = kst;
   g->smem = fixed + hdr + (size_t)kst * k_bytes;
@@ -177,34 +196,44 @@ int indexer_check(const void* q, const void* k, const void* w, const float* freq
   return KS_OK;
 }
 
-template <int H>
+template <int H, bool F8>
 int launch_indexer_scores(Device* dev, const CUtensorMap& qm, const CUtensorMap& km,
                           const IndexerScoreParams& p, const IndexerGeom& g, int grid,
                           cudaStream_t st) {
-  if (int rc = smem_optin(dev, reinterpret_cast<const void*>(indexer_score_kernel<H>),
+  if (int rc = smem_optin(dev, reinterpret_cast<const void*>(indexer_score_kernel<H, F8>),
                           "cudaFuncSetAttribute(indexer)"))
     return rc;
-  indexer_score_kernel<H><<<grid, IX_THREADS, g.smem, st>>>(qm, km, p);
+  indexer_score_kernel<H, F8><<<grid, IX_THREADS, g.smem, st>>>(qm, km, p);
   return launch_check("indexer_score_kernel launch");
 }
 
+// Score stage.  f8: q and k are e4m3 bytes, w is fp32 (head weight x query scale),
+// k_scale fp32 per key row; else q, k, w are bf16 and k_scale is unused.
 int indexer_scores_impl(const void* q, const void* k, int64_t k_batch_rows, const void* w,
                         const float* freqs, int64_t B, int64_t S, int64_t H, int64_t D,
                         int64_t T, int32_t rope_dim, int64_t pos0, int32_t causal,
-                        int32_t ratio, void* scores, int64_t score_ld, cudaStream_t st) {
+                        int32_t ratio, void* scores, int64_t score_ld, cudaStream_t st,
+                        bool f8 = false, const float* k_scale = nullptr) {
   Device* dev;
   if (int rc = device(&dev)) return rc;
   IndexerGeom g;
-  if (int rc = indexer_geom(B, S, H, D, &g)) return rc;
+  if (int rc = indexer_geom(B, S, H, D, f8, &g)) return rc;
   if (T == 0) return KS_OK;
   CUtensorMap qm, km;
-  if (int rc = make_map_bf16(&qm, q, D, (uint64_t)(B * S * H), D * 2, 64, IX_N)) return rc;
-  if (int rc = make_map_bf16(&km, k, D, (uint64_t)(B * k_batch_rows), D * 2, 64, IX_TILE_KEYS)) return rc;
+  if (f8) {
+    if (int rc = make_map_u8(&qm, q, D, (uint64_t)(B * S * H), D, 128, IX_N)) return rc;
+    if (int rc = make_map_u8(&km, k, D, (uint64_t)(B * k_batch_rows), D, 128, IX_TILE_KEYS)) return rc;
+  } else {
+    if (int rc = make_map_bf16(&qm, q, D, (uint64_t)(B * S * H), D * 2, 64, IX_N)) return rc;
+    if (int rc = make_map_bf16(&km, k, D, (uint64_t)(B * k_batch_rows), D * 2, 64, IX_TILE_KEYS)) return rc;
+  }
   IndexerScoreParams p{};
   p.freqs = freqs;
-  p.w = static_cast<const uint16_t*>(w);
+  p.w = f8 ? nullptr : static_cast<const uint16_t*>(w);
+  p.wf = f8 ? static_cast<const float*>(w) : nullptr;
+  p.k_scale = k_scale;
   p.w_bs = S * H;
-  p.w_vec16 = aligned(w, 16) ? 1 : 0;  // rows of H >= 16 bf16 are 16-byte multiples
+  p.w_vec16 = aligned(w, 16) ? 1 : 0;  // rows of H >= 16 elements are 16-byte multiples
   p.scores = static_cast<uint16_t*>(scores);
   p.score_ld = score_ld;
   p.B = (int)B; p.S = (int)S; p.H = (int)H; p.D = (int)D; p.T = (int)T; p.rd = rope_dim;
@@ -216,10 +245,17 @@ int indexer_scores_impl(const void* q, const void* k, int64_t k_batch_rows, cons
   p.status = dev->status;
   p.budget_ns = wait_budget_ns();
   const int grid = g.n_items < dev->num_sms ? g.n_items : dev->num_sms;
+  if (f8) {
+    switch (H) {
+      case 16: return launch_indexer_scores<16, true>(dev, qm, km, p, g, grid, st);
+      case 32: return launch_indexer_scores<32, true>(dev, qm, km, p, g, grid, st);
+      default: return launch_indexer_scores<64, true>(dev, qm, km, p, g, grid, st);
+    }
+  }
   switch (H) {
-    case 16: return launch_indexer_scores<16>(dev, qm, km, p, g, grid, st);
-    case 32: return launch_indexer_scores<32>(dev, qm, km, p, g, grid, st);
-    default: return launch_indexer_scores<64>(dev, qm, km, p, g, grid, st);
+    case 16: return launch_indexer_scores<16, false>(dev, qm, km, p, g, grid, st);
+    case 32: return launch_indexer_scores<32, false>(dev, qm, km, p, g, grid, st);
+    default: return launch_indexer_scores<64, false>(dev, qm, km, p, g, grid, st);
   }
 }
 
@@ -525,6 +561,74 @@ int ks_dsa(const void* q_ix, const void* k_ix, int64_t k_batch_rows, const void*
     return rc;
   return sparse_attn_impl(q_sa, kv, attn_sink, idx_out, out, B, S, H_sa, D_sa, N, K, 0, dv,
                           softmax_scale, st);
+}
+
+int ks_quant_fp8_rows(const void* x, void* x8, float* scale, int64_t rows, int32_t D,
+                      void* stream) {
+  Device* dev;
+  if (int rc = device(&dev)) return rc;
+  if (!x || !x8 || !scale) return fail(KS_ERR_INVALID, "quant_fp8_rows: null pointer");
+  if (rows < 0 || D < 4 || D % 4) return fail(KS_ERR_INVALID, "quant_fp8_rows: rows=%lld D=%d (D a multiple of 4)", (long long)rows, D);
+  if (!aligned(x, 8) || !aligned(x8, 4) || !aligned(scale, 4))
+    return fail(KS_ERR_ALIGNMENT, "quant_fp8_rows: x must be 8-byte and x8, scale 4-byte aligned");
+  if (rows == 0) return KS_OK;
+  const int64_t blocks = (rows + QF_WARPS - 1) / QF_WARPS;
+  if (blocks > 0x7FFFFFFFll) return fail(KS_ERR_UNSUPPORTED, "quant_fp8_rows: too many rows");
+  quant_fp8_rows_kernel<<<(unsigned)blocks, QF_WARPS * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(x), static_cast<uint8_t*>(x8), scale, rows, D);
+  return launch_check("quant_fp8_rows_kernel launch");
+}
+
+namespace {
+int indexer_fp8_check(const void* q8, const void* k8, const float* w, const float* k_scale,
+                      int64_t B, int64_t S, int64_t H, int64_t D, int64_t T, int32_t ratio,
+                      int64_t k_batch_rows) {
+  if (!q8 || !k8 || !w || !k_scale) return fail(KS_ERR_INVALID, "indexer_fp8: null input pointer");
+  if (B < 1 || S < 1 || T < 0) return fail(KS_ERR_INVALID, "indexer_fp8: bad sizes B=%lld S=%lld T=%lld", (long long)B, (long long)S, (long long)T);
+  if (!(H == 16 || H == 32 || H == 64)) return fail(KS_ERR_UNSUPPORTED, "indexer_fp8: H=%lld (supported: 16, 32, 64)", (long long)H);
+  if (D != 128) return fail(KS_ERR_UNSUPPORTED, "indexer_fp8: D=%lld (supported: 128)", (long long)D);
+  if (T > 65536) return fail(KS_ERR_UNSUPPORTED, "indexer_fp8: T=%lld > 65536", (long long)T);
+  if (ratio < 1) return fail(KS_ERR_INVALID, "indexer_fp8: ratio=%d", ratio);
+  if (k_batch_rows < T) return fail(KS_ERR_INVALID, "indexer_fp8: k_batch_rows < T");
+  if (!aligned(q8, 16) || !aligned(k8, 16) || !aligned(w, 4) || !aligned(k_scale, 4))
+    return fail(KS_ERR_ALIGNMENT, "indexer_fp8: q8, k8 must be 16-byte and w, k_scale 4-byte aligned");
+  if (B * S * H >= (1ll << 31) || B * k_batch_rows >= (1ll << 31))
+    return fail(KS_ERR_UNSUPPORTED, "indexer_fp8: too many rows for 32-bit TMA coordinates");
+  return KS_OK;
+}
+}  // namespace
+
+int ks_indexer_fp8_scores(const void* q8, const void* k8, int64_t k_batch_rows, const float* w,
+                          const float* k_scale, int64_t B, int64_t S, int64_t H, int64_t D,
+                          int64_t T, int64_t pos0, int32_t causal, int32_t ratio, void* scores,
+                          int64_t score_ld, void* stream) {
+  if (int rc = indexer_fp8_check(q8, k8, w, k_scale, B, S, H, D, T, ratio, k_batch_rows)) return rc;
+  if (!scores || score_ld < T || score_ld % 8 || !aligned(scores, 16))
+    return fail(KS_ERR_INVALID, "indexer_fp8_scores: scores must be 16-byte aligned with score_ld >= T, multiple of 8");
+  return indexer_scores_impl(q8, k8, k_batch_rows, w, nullptr, B, S, H, D, T, 0, pos0, causal,
+                             ratio, scores, score_ld, static_cast<cudaStream_t>(stream), true,
+                             k_scale);
+}
+
+int ks_indexer_fp8(const void* q8, const void* k8, int64_t k_batch_rows, const float* w,
+                   const float* k_scale, int64_t B, int64_t S, int64_t H, int64_t D, int64_t T,
+                   int64_t pos0, int32_t causal, int32_t ratio, int32_t topk, int64_t offset,
+                   void* out, int32_t out_dtype, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  if (int rc = indexer_fp8_check(q8, k8, w, k_scale, B, S, H, D, T, ratio, k_batch_rows)) return rc;
+  if (topk < 1 || topk > 4096) return fail(KS_ERR_UNSUPPORTED, "indexer_fp8: topk=%d (1..4096)", topk);
+  if (!out) return fail(KS_ERR_INVALID, "indexer_fp8: out is null");
+  if (T == 0) return KS_OK;
+  const size_t need = ks_indexer_workspace_size(B, S, T);
+  if (!workspace || workspace_bytes < need)
+    return fail(KS_ERR_WORKSPACE, "indexer_fp8: workspace of %zu bytes needed", need);
+  if (!aligned(workspace, 256)) return fail(KS_ERR_ALIGNMENT, "indexer_fp8: workspace must be 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t ld = round_up(T, 8);
+  if (int rc = indexer_scores_impl(q8, k8, k_batch_rows, w, nullptr, B, S, H, D, T, 0, pos0,
+                                   causal, ratio, workspace, ld, st, true, k_scale))
+    return rc;
+  return topk_impl(workspace, ld, B, S, T, pos0, causal, ratio, topk, offset, out, out_dtype, st);
 }
 
 int ks_device_status(void* stream) {

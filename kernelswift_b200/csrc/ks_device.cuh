@@ -335,6 +335,17 @@ __device__ __forceinline__ void umma_bf16_ss_cg2(uint32_t d_tmem, uint64_t adesc
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, e4m3 (fp8) inputs, fp32 accumulate; one
+// instruction contracts K = 32 elements (32 bytes of each K-major row).
+__device__ __forceinline__ void umma_f8_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;"
+      " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // cta_group::2 MMA with descriptors passed as (low, high) words: the start address
 // sits in the low 14 bits, so per-MMA offsets are single 32-bit adds.
 __device__ __forceinline__ void umma_cg2_w(uint32_t d, uint32_t alo, uint32_t ahi, uint32_t blo,
@@ -431,6 +442,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_ma
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
          ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
+}
+
+// Instruction descriptor, kind::f8f6f4: e4m3 A and B (format code 0), fp32 D,
+// both K-major; same field positions as idesc_bf16_f32.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // ------------------------------------------------------------------ bf16 arithmetic

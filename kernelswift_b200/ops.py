@@ -9,6 +9,8 @@ These are the B200 counterparts of the reference's torch extension ops
   (indexer_torch.cpp:100-268), fused behind one call
 * ``indexer_scores`` / ``topk_rows`` expose the two indexer stages separately.
 * ``dsa`` runs the indexer's int32 top-k straight into ``sparse_attn`` in one call.
+* ``quant_fp8_rows`` / ``indexer_topk_fp8`` / ``indexer_scores_fp8``: the FP8 indexer
+  (``ModelArgs.dtype = "fp8"``), which the reference declares but does not implement.
 
 Every op runs on the current CUDA stream of its input's device, validates its
 arguments like the reference (a ``RuntimeError`` on a bad dtype, device, shape
@@ -243,6 +245,92 @@ def dsa(q_ix: torch.Tensor, k_ix: torch.Tensor, w: torch.Tensor, freqs: torch.Te
                            _ptr(out), _ptr(workspace), workspace.numel() * workspace.element_size(),
                            _stream(q_ix)), "ks_dsa")
     return out, idx_out
+
+
+_FP8 = (torch.float8_e4m3fn, torch.uint8)
+
+
+def quant_fp8_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """e4m3 quantisation of bf16 rows [..., D] with one power-of-two ("ue8m0")
+    scale per row: returns (x8 float8_e4m3fn [..., D], scale fp32 [...]), with
+    x ~= x8 * scale.  The input side of ``indexer_topk_fp8``."""
+    if x.dtype != torch.bfloat16 or x.dim() < 1:
+        raise RuntimeError("quant_fp8_rows: x must be bfloat16 [..., D]")
+    _require_cuda("quant_fp8_rows", x)
+    D = x.shape[-1]
+    x8 = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    scale = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        check(lib().ks_quant_fp8_rows(_ptr(x), _ptr(x8), _ptr(scale), x.numel() // max(D, 1), D,
+                                      _stream(x)), "ks_quant_fp8_rows")
+    return x8, scale
+
+
+def _indexer_fp8_args(q8, k8, w, k_scale, T):
+    if q8.dtype not in _FP8 or k8.dtype not in _FP8:
+        raise RuntimeError("indexer_fp8: q8 and k8 must be float8_e4m3fn (or their uint8 bytes)")
+    if w.dtype != torch.float32 or k_scale.dtype != torch.float32:
+        raise RuntimeError("indexer_fp8: w and k_scale must be float32")
+    if q8.dim() != 4 or k8.dim() != 3 or w.dim() != 3 or k_scale.dim() != 2:
+        raise RuntimeError("indexer_fp8: expected q8 [b,s,h,d], k8 [b,t,d], w [b,s,h], k_scale [b,t]")
+    B, S, H, D = q8.shape
+    if k8.shape[0] < B or k8.shape[2] != D or k8.shape[1] < T:
+        raise RuntimeError("indexer_fp8: k8 shape mismatch")
+    if tuple(w.shape) != (B, S, H) or tuple(k_scale.shape) != tuple(k8.shape[:2]):
+        raise RuntimeError("indexer_fp8: w / k_scale shape mismatch")
+    _require_cuda("indexer_fp8", q8, k8[:B], w, k_scale)
+    return B, S, H, D
+
+
+def indexer_topk_fp8(q8: torch.Tensor, k8: torch.Tensor, w: torch.Tensor, k_scale: torch.Tensor,
+                     T: int, topk: int, ratio: int = 1, causal: bool = True, offset: int = 0,
+                     pos0: int = 0, out_dtype: torch.dtype = torch.int64,
+                     out: torch.Tensor | None = None,
+                     workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """FP8 indexer top-k (ModelArgs.dtype = "fp8", baseline/indexer.py:14-17):
+    e4m3 queries q8 [B,S,H,128] (rotated, then quantised per (token, head)) and
+    keys k8 [B,Tk>=T,128] with per-key scales k_scale [B,Tk]; w fp32 [B,S,H] =
+    head weight x query scale.  Scores bf16(k_scale * sum_h relu(q8.k8) * w), then
+    the mask, top-k and post-processing of ``indexer_topk``."""
+    B, S, H, D = _indexer_fp8_args(q8, k8, w, k_scale, T)
+    kk = min(int(topk), int(T))
+    if out is None:
+        out = torch.empty((B, S, kk), dtype=out_dtype, device=q8.device)
+    elif out.dtype not in (torch.int32, torch.int64):
+        raise RuntimeError("indexer_fp8: out must be int32 or int64")
+    else:
+        _check_out("indexer_fp8", out, (B, S, kk), out.dtype, q8.device)
+    if T == 0:
+        return out
+    need = indexer_workspace_size(B, S, T)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q8.device)
+    else:
+        _check_workspace("indexer_fp8", workspace, need, q8.device)
+    with torch.cuda.device(q8.device):
+        check(lib().ks_indexer_fp8(_ptr(q8), _ptr(k8), k8.shape[1], _ptr(w), _ptr(k_scale), B, S,
+                                   H, D, int(T), int(pos0), int(bool(causal)), int(ratio),
+                                   int(topk), int(offset), _ptr(out),
+                                   KS_INT64 if out.dtype == torch.int64 else KS_INT32,
+                                   _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                   _stream(q8)), "ks_indexer_fp8")
+    return out
+
+
+def indexer_scores_fp8(q8: torch.Tensor, k8: torch.Tensor, w: torch.Tensor,
+                       k_scale: torch.Tensor, T: int, ratio: int = 1, causal: bool = True,
+                       pos0: int = 0) -> torch.Tensor:
+    """Score stage of ``indexer_topk_fp8`` alone: bf16 [B, S, ld] laid out as
+    ``indexer_scores``."""
+    B, S, H, D = _indexer_fp8_args(q8, k8, w, k_scale, T)
+    ld = (int(T) + 7) // 8 * 8
+    scores = torch.full((B, S, ld), float("-inf"), dtype=torch.bfloat16, device=q8.device)
+    with torch.cuda.device(q8.device):
+        check(lib().ks_indexer_fp8_scores(_ptr(q8), _ptr(k8), k8.shape[1], _ptr(w), _ptr(k_scale),
+                                          B, S, H, D, int(T), int(pos0), int(bool(causal)),
+                                          int(ratio), _ptr(scores), ld, _stream(q8)),
+              "ks_indexer_fp8_scores")
+    return scores
 
 
 def indexer_scores(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, freqs: torch.Tensor | None,

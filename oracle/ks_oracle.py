@@ -15,6 +15,16 @@ were generated here with 2.11.0 CPU):
 * ``indexer_scores``<- baseline/indexer.py:170-183 (+ causal mask :185-193)
 * ``topk_stable`` / ``indexer_postprocess`` <- baseline/indexer.py:195-205
 
+FP8 indexer (``e4m3_*``, ``quant_fp8_rows``, ``indexer_scores_fp8``): the
+reference declares ``ModelArgs.dtype = "fp8"`` and ``scale_fmt = "ue8m0"``
+(baseline/indexer.py:14-17) but its bf16 baseline never uses them and no FP8
+kernel exists in the repository, so there is no reference output to pin these
+against.  They restate the published e4m3 format (OCP 8-bit floating point:
+1 sign, 4 exponent bits with bias 7, 3 mantissa bits, no infinities, largest
+finite 448) and the operator contract stated in include/ks_b200.h; the e4m3
+tables are checked exhaustively in tests/test_fp8_cpu.py.  Parity of the FP8
+path is therefore "unpinned" against the reference.
+
 The oracle is pinned against the golden fixtures in ``tests/golden`` that
 ``tests/golden/make_golden.py`` produced by running the reference's own modules
 (see ``tests/test_oracle_golden.py``).
@@ -215,3 +225,82 @@ def indexer_forward(q_pre: np.ndarray, k: np.ndarray, w: np.ndarray, freqs: np.n
     kk = min(topk, T)
     idx = topk_stable(sc, kk)
     return indexer_postprocess(idx, S, s0, causal, ratio, offset), sc
+
+
+# ---------------------------------------------------------------- FP8 (e4m3) indexer
+def _e4m3_table() -> np.ndarray:
+    """float32 value of every e4m3 code (NaN for 0x7F and 0xFF)."""
+    v = np.empty(256, np.float32)
+    for c in range(256):
+        sgn = -1.0 if c & 0x80 else 1.0
+        e, m = (c >> 3) & 0xF, c & 7
+        if e == 0xF and m == 7:
+            v[c] = np.nan
+        elif e == 0:
+            v[c] = sgn * (m / 8.0) * 2.0 ** -6
+        else:
+            v[c] = sgn * (1.0 + m / 8.0) * 2.0 ** (e - 7)
+    return v
+
+
+E4M3 = _e4m3_table()
+_POS = E4M3[:0x7F]          # codes 0x00..0x7E: +0 .. 448, increasing
+
+
+def e4m3_decode(codes: np.ndarray) -> np.ndarray:
+    return E4M3[np.asarray(codes, np.uint8)]
+
+
+def e4m3_encode(x: np.ndarray) -> np.ndarray:
+    """float32 -> e4m3 codes, round to nearest (ties to the even code) and
+    saturation to +-448 (the cvt.rn.satfinite rule); the sign of zero is kept."""
+    x = np.asarray(x, np.float32)
+    a = np.abs(x)
+    hi = np.clip(np.searchsorted(_POS, a, side="left"), 0, len(_POS) - 1)  # first >= a
+    lo = np.maximum(hi - 1, 0)
+    d_lo = a - _POS[lo]
+    d_hi = _POS[hi] - a
+    pick_hi = (d_hi < d_lo) | ((d_hi == d_lo) & (hi % 2 == 0))
+    code = np.where(pick_hi, hi, lo)
+    code = np.where(a >= _POS[-1], len(_POS) - 1, code)  # saturate
+    return (code | np.where(np.signbit(x), 0x80, 0)).astype(np.uint8)
+
+
+def quant_fp8_rows(x_bits: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Rows of bf16 bits [..., D] -> (e4m3 codes [..., D], fp32 scales [...]):
+    scale = smallest power of two >= max(amax, 1e-4) / 448, codes of x / scale."""
+    x = bf16_to_f32(x_bits)
+    amax = np.maximum(np.abs(x).max(axis=-1), np.float32(1e-4)).astype(np.float32)
+    v = (amax / np.float32(448.0)).astype(np.float32)
+    m, e = np.frexp(v)                               # v = m * 2^e, m in [0.5, 1)
+    s = np.where(m == 0.5, v, np.ldexp(np.float32(1.0), e)).astype(np.float32)
+    return e4m3_encode((x / s[..., None]).astype(np.float32)), s
+
+
+def indexer_scores_fp8(q8: np.ndarray, k8: np.ndarray, w: np.ndarray, k_scale: np.ndarray,
+                       causal: bool, ratio: int, s0: int = 0) -> np.ndarray:
+    """FP8 indexer scores (operator contract of ks_indexer_fp8) for rows s0..:
+    bf16( k_scale[t] * sum_h fp32(relu(dot_h) * w_h) ) with the head sum in fp32,
+    heads in order, and the causal mask of baseline/indexer.py:185-193.
+    q8 [B,S,H,D] and k8 [B,T,D] e4m3 codes, w [B,S,H] fp32, k_scale [B,T] fp32.
+    The dot products are exact (float64) rounded once to fp32."""
+    B, S, H, D = q8.shape
+    T = k8.shape[1]
+    out = np.empty((B, S, T), np.uint16)
+    lim = indexer_limits(S, s0, causal, ratio, T)
+    for b in range(B):
+        kf = e4m3_decode(k8[b]).astype(np.float64)          # [T, D]
+        for r0 in range(0, S, 16):
+            r1 = min(S, r0 + 16)
+            qf = e4m3_decode(q8[b, r0:r1]).astype(np.float64).reshape(-1, D)
+            dot = (qf @ kf.T).astype(np.float32).reshape(r1 - r0, H, T)
+            rel = np.maximum(dot, np.float32(0.0))
+            acc = np.zeros((r1 - r0, T), np.float32)
+            wf = np.asarray(w[b, r0:r1], np.float32)
+            for h in range(H):
+                acc = (acc + (rel[:, h, :] * wf[:, h:h + 1]).astype(np.float32)).astype(np.float32)
+            res = f32_to_bf16((acc * np.asarray(k_scale[b], np.float32)[None, :]).astype(np.float32))
+            for i in range(r1 - r0):
+                res[i, lim[r0 + i]:] = NEG_INF_BF16
+            out[b, r0:r1] = res
+    return out
