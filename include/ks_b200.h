@@ -144,6 +144,26 @@ int ks_dsa(const void* q_ix, const void* k_ix, int64_t k_batch_rows, const void*
            void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The indexer's projections with their follow-up arithmetic fused: the
+ * producer of ks_indexer's q (rotated) and w (scaled) inputs.
+ *   out[m, n] = bf16( sum_k a[m, k] * w[n, k] )            a bf16 [M, K], w bf16 [N, K]
+ * (F.linear: fp32 accumulation, bf16 result), then
+ *   rope_dim > 0: in every head_dim-wide group of columns the last rope_dim are
+ *                 rotated as interleaved pairs with freqs[m % S] ([S, rope_dim/2, 2]
+ *                 fp32 cos, sin), products and sums in fp32, result bf16
+ *   apply_scale:  out = bf16( float(out) * scale )
+ * Computes q = wq_b(qr) + RoPE (baseline/indexer.py:170-172, 114-129; then call
+ * ks_indexer with rope_dim = 0) and weights = weights_proj(x) * scale
+ * (baseline/indexer.py:173-175) on the tensor cores.  N % 16 == 0, K % 8 == 0,
+ * pointers 16-byte aligned.  Replaces the reference's torch-side projections
+ * and its RoPE op (optimized/indexer_project/indexer.py:196-200,
+ * optimized/indexer_project/op_extension/indexer_torch.cpp:100-172).
+ */
+int ks_proj_rope(const void* a, const void* w, void* out, int64_t M, int64_t N, int64_t K,
+                 int32_t head_dim, int32_t rope_dim, const float* freqs, int64_t S, float scale,
+                 int32_t apply_scale, void* stream);
+
+/*
  * e4m3 (fp8) quantisation of bf16 rows [rows, D] with one power-of-two scale
  * per row (the "ue8m0" scale format of ModelArgs, baseline/indexer.py:15):
  * scale[r] = the smallest power of two >= max(max_i |x[r,i]|, 1e-4) / 448 and

@@ -47,6 +47,8 @@ SIGNATURES = {
     "ks_dsa": (ctypes.c_int, [_vp, _vp, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                               _c_i32, _c_i64, _c_i32, _c_i32, _c_i32, _c_i64, _vp, _vp, _c_i64, _vp,
                               _c_i64, _c_i64, _c_i64, _c_f32, _vp, _vp, _vp, _sz, _vp]),
+    "ks_proj_rope": (ctypes.c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i32, _c_i32, _vp,
+                                    _c_i64, _c_f32, _c_i32, _vp]),
     "ks_quant_fp8_rows": (ctypes.c_int, [_vp, _vp, _vp, _c_i64, _c_i32, _vp]),
     "ks_indexer_fp8": (ctypes.c_int, [_vp, _vp, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64,
                                       _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i64, _vp, _c_i32,

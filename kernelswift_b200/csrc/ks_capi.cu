@@ -12,6 +12,7 @@
 #include "ks_b200.h"
 #include "ks_device.cuh"
 #include "indexer_score.cuh"
+#include "proj_gemm.cuh"
 #include "quant_fp8.cuh"
 #include "sinkhorn.cuh"
 #include "sparse_attn.cuh"
@@ -561,6 +562,59 @@ int ks_dsa(const void* q_ix, const void* k_ix, int64_t k_batch_rows, const void*
     return rc;
   return sparse_attn_impl(q_sa, kv, attn_sink, idx_out, out, B, S, H_sa, D_sa, N, K, 0, dv,
                           softmax_scale, st);
+}
+
+int ks_proj_rope(const void* a, const void* w, void* out, int64_t M, int64_t N, int64_t K,
+                 int32_t head_dim, int32_t rope_dim, const float* freqs, int64_t S, float scale,
+                 int32_t apply_scale, void* stream) {
+  Device* dev;
+  if (int rc = device(&dev)) return rc;
+  if (!a || !w || !out) return fail(KS_ERR_INVALID, "proj_rope: null pointer");
+  if (M < 0 || N < 16 || K < 8 || N % 16 || K % 8)
+    return fail(KS_ERR_INVALID, "proj_rope: M=%lld N=%lld K=%lld (N a multiple of 16, K of 8)", (long long)M, (long long)N, (long long)K);
+  if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) return fail(KS_ERR_UNSUPPORTED, "proj_rope: too large");
+  if (rope_dim < 0 || rope_dim % 2) return fail(KS_ERR_INVALID, "proj_rope: rope_dim=%d must be even", rope_dim);
+  if (rope_dim > 0) {
+    if (head_dim < rope_dim || head_dim % 16 || N % head_dim)
+      return fail(KS_ERR_INVALID, "proj_rope: head_dim=%d must be a multiple of 16 that divides N and holds rope_dim", head_dim);
+    if (!freqs || S < 1 || !aligned(freqs, 8)) return fail(KS_ERR_INVALID, "proj_rope: freqs [S, rope_dim/2, 2] (8-byte aligned) required");
+  }
+  if (!aligned(a, 16) || !aligned(w, 16) || !aligned(out, 16))
+    return fail(KS_ERR_ALIGNMENT, "proj_rope: a, w, out must be 16-byte aligned");
+  if (M == 0) return KS_OK;
+  int n_tile = 256;
+  while (N % n_tile) n_tile >>= 1;  // N % 16 == 0, so this stops at 16 or above
+  ProjParams p{};
+  p.out = static_cast<uint16_t*>(out);
+  p.freqs = freqs;
+  p.M = (int)M; p.N = (int)N; p.K = (int)K; p.S = (int)(S > 0 ? S : 1);
+  p.n_tile = n_tile;
+  p.hd = rope_dim > 0 ? head_dim : 16;
+  p.rd = rope_dim;
+  p.scale = scale;
+  p.apply_scale = apply_scale ? 1 : 0;
+  const size_t st_bytes = (size_t)PG_TILE_M * 128 + (size_t)n_tile * 128;
+  int stages = (int)((232448 - 2048) / st_bytes);
+  if (stages > PG_MAX_STAGES) stages = PG_MAX_STAGES;
+  p.stages = stages;
+  p.tiles_m = (int)((M + PG_TILE_M - 1) / PG_TILE_M);
+  p.tiles_n = (int)(N / n_tile);
+  p.status = dev->status;
+  p.budget_ns = wait_budget_ns();
+  // at least half of the shared memory, so two CTAs never share an SM (each
+  // allocates all 512 TMEM columns)
+  size_t smem = 1024 + 1024 + (size_t)stages * st_bytes;
+  if (smem < 120 * 1024) smem = 120 * 1024;
+  CUtensorMap am, bm;
+  if (int rc = make_map_bf16(&am, a, K, (uint64_t)M, K * 2, 64, PG_TILE_M)) return rc;
+  if (int rc = make_map_bf16(&bm, w, K, (uint64_t)N, K * 2, 64, n_tile)) return rc;
+  if (int rc = smem_optin(dev, reinterpret_cast<const void*>(proj_gemm_kernel),
+                          "cudaFuncSetAttribute(proj_gemm)"))
+    return rc;
+  const int64_t tiles = (int64_t)p.tiles_m * p.tiles_n;
+  const int grid = (int)(tiles < dev->num_sms ? tiles : dev->num_sms);
+  proj_gemm_kernel<<<grid, PG_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(am, bm, p);
+  return launch_check("proj_gemm_kernel launch");
 }
 
 int ks_quant_fp8_rows(const void* x, void* x8, float* scale, int64_t rows, int32_t D,

@@ -1,0 +1,200 @@
+// The indexer's projections on tcgen05 with their follow-up arithmetic fused into
+// the epilogue: the producer of the score kernel's inputs.
+//
+// Semantics follow baseline/indexer.py:170-175 (+ RoPE, :114-129,172):
+//   y[m, n] = bf16( sum_k a[m, k] * w[n, k] )          F.linear, bf16 in, fp32 accumulate
+//   rope:  the last `rd` of every `hd` columns are rotated as interleaved pairs
+//          with freqs[m % S] (fp32 products and sums rounded separately, result
+//          rounded to bf16), as apply_rotary_emb does to q[..., -rd:]
+//   scale: y = bf16( float(y) * scale ), as weights_proj(x) * (D^-0.5 H^-0.5)
+// so q = wq_b(qr) leaves this kernel already rotated (the score kernel then runs
+// without RoPE) and the head weights leave it scaled.  Fusing the projection into
+// the score kernel itself would make every 4-token work item stream all of w
+// (16 MB for 64 heads x 128 dims x 1024) from L2; as its producer the GEMM reads
+// each operand tile once per output tile.
+//
+// One persistent CTA per SM, 6 warps: warp 0 TMA producer (A tile 128 x 64 and
+// B tile N_TILE x 64 per stage, 128-byte swizzle), warp 1 TMEM owner and MMA
+// issuer (M = 128, N = N_TILE, K = 16 per instruction, fp32 accumulators double
+// buffered in TMEM), warps 2-5 epilogue (thread = output row = TMEM lane).
+#pragma once
+#include "ks_device.cuh"
+
+namespace ks {
+
+constexpr int PG_THREADS = 192;
+constexpr int PG_EPI_WARP0 = 2;
+constexpr int PG_TILE_M = 128;
+constexpr int PG_MAX_STAGES = 8;
+
+struct ProjParams {
+  uint16_t* out;        // bf16 [M, N]
+  const float* freqs;   // [S, rd/2, 2] (cos, sin), row m uses freqs[m % S]
+  int32_t M, N, K, S;
+  int32_t n_tile;       // 16..256, multiple of 16, divides N
+  int32_t hd, rd;       // head dim and rotated dims (rd = 0: no RoPE)
+  float scale;          // applied after the bf16 rounding when apply_scale
+  int32_t apply_scale;
+  int32_t stages;
+  int32_t tiles_m, tiles_n;
+  int* status;
+  uint64_t budget_ns;
+};
+
+struct PgShared {
+  uint64_t full[PG_MAX_STAGES], empty[PG_MAX_STAGES];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+static_assert(sizeof(PgShared) <= 1024, "PgShared exceeds its header");
+
+__global__ void __launch_bounds__(PG_THREADS, 1)
+    proj_gemm_kernel(const __grid_constant__ CUtensorMap amap,
+                     const __grid_constant__ CUtensorMap bmap, ProjParams p) {
+  extern __shared__ uint8_t pg_raw[];
+  const uint32_t raw_addr = smem_u32(pg_raw);
+  uint8_t* smem = pg_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  PgShared* sh = reinterpret_cast<PgShared*>(smem);
+  const uint32_t a_bytes = PG_TILE_M * 128, b_bytes = (uint32_t)p.n_tile * 128;
+  const uint32_t st_bytes = a_bytes + b_bytes;
+  uint8_t* stage0 = smem + 1024;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_k = (p.K + 63) / 64;
+  const int n_tiles = p.tiles_m * p.tiles_n;
+  WaitCtx wc{&sh->abort, p.status, p.budget_ns};
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.stages; ++i) {
+      mbar_init(&sh->full[i], 1);
+      mbar_init(&sh->empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh->acc_full[i], 1);
+      mbar_init(&sh->acc_empty[i], 4);  // the four epilogue warps
+    }
+    mbar_init(&sh->drain, 1);
+    sh->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<1>(&sh->tmem_base, 512);
+    tmem_relinquish<1>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&amap);
+      tma_prefetch_desc(&bmap);
+      uint32_t c = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
+        for (int kc = 0; kc < n_k; ++kc, ++c) {
+          const int st = (int)(c % (uint32_t)p.stages);
+          if (!(ok = mbar_wait(&sh->empty[st], ((c / p.stages) & 1) ^ 1, wc))) break;
+          uint8_t* sa = stage0 + st * st_bytes;
+          mbar_expect_tx(&sh->full[st], st_bytes);
+          tma_load_2d(&amap, &sh->full[st], sa, kc * 64, tm * PG_TILE_M);
+          tma_load_2d(&bmap, &sh->full[st], sa + a_bytes, kc * 64, tn * p.n_tile);
+        }
+      }
+      // drain: every load issued has landed before the CTA exits
+      for (uint32_t i = (c > (uint32_t)p.stages ? c - p.stages : 0); i < c; ++i)
+        mbar_wait(&sh->full[i % p.stages], (i / p.stages) & 1, wc, false, true);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(PG_TILE_M, p.n_tile, false, false);
+      uint32_t c = 0, ac = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++ac) {
+        const int as = ac & 1;
+        if (!(ok = mbar_wait(&sh->acc_empty[as], ((ac >> 1) & 1) ^ 1, wc))) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + as * 256;
+        for (int kc = 0; kc < n_k; ++kc, ++c) {
+          const int st = (int)(c % (uint32_t)p.stages);
+          if (!(ok = mbar_wait_inl(&sh->full[st], (c / p.stages) & 1, wc))) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(stage0 + st * st_bytes);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = sdesc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(sa + a_bytes + kk * 32, 16, 1024);
+            umma_bf16_ss(d_tmem, ad, bd, idesc, (kc | kk) ? 1u : 0u);
+          }
+          umma_commit(&sh->empty[st]);
+        }
+        if (!ok) break;
+        umma_commit(&sh->acc_full[as]);
+      }
+      umma_commit(&sh->drain);
+      mbar_wait(&sh->drain, 0, wc, false, true);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes [32 quarter, +32)
+    const int row_in_tile = quarter * 32 + lane;
+    const int half_rd = p.rd / 2;
+    const int rope0 = p.hd - p.rd;  // first rotated column of a head
+    uint32_t ac = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++ac) {
+      const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
+      const int as = ac & 1;
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&sh->acc_full[as], (ac >> 1) & 1, wc))) break;
+      tc_fence_after();
+      const int m = tm * PG_TILE_M + row_in_tile;
+      const bool row_ok = m < p.M;
+      const float* fr = p.freqs + (int64_t)(row_ok ? m % p.S : 0) * p.rd;
+      uint16_t* orow = p.out + (int64_t)m * p.N + (int64_t)tn * p.n_tile;
+      const uint32_t tbase = tmem + as * 256 + ((uint32_t)(quarter * 32) << 16);
+      for (int c = 0; c < p.n_tile; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(tbase + c, r);
+        tmem_wait_ld();
+        uint32_t o[8];
+        const int d0 = (tn * p.n_tile + c) % p.hd;  // head-local column of r[0]
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          // bf16 rounding of the GEMM output (F.linear returns bf16)
+          uint32_t v = cvt_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+          const int d = d0 + 2 * i;
+          if (p.rd > 0 && d >= rope0 && row_ok) {
+            const int j = (d - rope0) >> 1;
+            const float2 cs = __ldg(reinterpret_cast<const float2*>(fr) + j);
+            const float xr = bf16lo_f32(v), xi = bf16hi_f32(v);
+            const float re = __fsub_rn(__fmul_rn(xr, cs.x), __fmul_rn(xi, cs.y));
+            const float im = __fadd_rn(__fmul_rn(xr, cs.y), __fmul_rn(xi, cs.x));
+            v = cvt_bf16x2(re, im);
+          }
+          if (p.apply_scale)
+            v = cvt_bf16x2(__fmul_rn(bf16lo_f32(v), p.scale), __fmul_rn(bf16hi_f32(v), p.scale));
+          o[i] = v;
+        }
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c);
+          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->acc_empty[as]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc<1>(tmem, 512);
+}
+
+}  // namespace ks

@@ -4,10 +4,12 @@ compress_ratio=4)``, submodules ``wq_b``/``weights_proj``, buffers
 ``kv_cache``/``freqs_cis``, ``forward(x, qr, start_pos, offset)`` returning
 int64 indices, ``get_inputs``, ``get_init_inputs``).
 
-The two projections run in torch, as in the reference
-(optimized/indexer_project/indexer.py:197,200); RoPE, the score GEMM, the
-ReLU-weighted head reduction, the causal mask, the exact top-k and the
--1/offset post-processing run in libks_b200.so.
+The two projections run on the tensor cores with RoPE and the weight scaling
+fused into their epilogue (``ops.proj_rope``; ``fused_projections = False``
+keeps them in torch, as the reference does,
+optimized/indexer_project/indexer.py:197,200); the score GEMM, the ReLU-weighted
+head reduction, the causal mask, the exact top-k and the -1/offset
+post-processing run in libks_b200.so.
 """
 import math
 from dataclasses import dataclass
@@ -136,18 +138,34 @@ class ModelNew(nn.Module):
         self.register_buffer("kv_cache", kv_cache)
         self.register_buffer("freqs_cis", freqs_cis)
 
+    # True: the projections run in libks_b200 (ops.proj_rope: tcgen05 GEMM with the
+    # RoPE and the weight scaling in its epilogue); False: in torch, as the
+    # reference does (optimized/indexer_project/indexer.py:196-200), with RoPE in
+    # the score kernel
+    fused_projections = True
+
     def forward(self, x: torch.Tensor, qr: torch.Tensor, start_pos: int, offset: int) -> torch.Tensor:
+        ops = _ops()
         batch_size, seq_len, _ = x.size()
         end_pos = start_pos + seq_len
         ratio = self.compress_ratio
-        q = self.wq_b(qr).unflatten(-1, (self.n_local_heads, self.head_dim))
-        weights = self.weights_proj(x) * (self.softmax_scale * self.n_heads ** -0.5)
         fc = self.freqs_cis[start_pos:end_pos]
-        freqs = torch.view_as_real(fc) if fc.is_complex() else fc
-        return _ops().indexer_topk(
-            q.contiguous(), self.kv_cache[:batch_size], weights.contiguous(),
-            freqs.float().contiguous(), rope_dim=self.rope_head_dim, T=end_pos // ratio,
-            topk=self.index_topk, ratio=ratio, causal=start_pos == 0, offset=offset, pos0=0)
+        freqs = (torch.view_as_real(fc) if fc.is_complex() else fc).float().contiguous()
+        scale = self.softmax_scale * self.n_heads ** -0.5
+        if self.fused_projections:
+            q = ops.proj_rope(qr.contiguous(), self.wq_b.weight, self.head_dim,
+                              self.rope_head_dim, freqs)
+            weights = ops.proj_rope(x.contiguous(), self.weights_proj.weight, scale=scale)
+            rope_dim, freqs = 0, None
+        else:
+            q = self.wq_b(qr)
+            weights = self.weights_proj(x) * scale
+            rope_dim = self.rope_head_dim
+        q = q.unflatten(-1, (self.n_local_heads, self.head_dim))
+        return ops.indexer_topk(
+            q.contiguous(), self.kv_cache[:batch_size], weights.contiguous(), freqs,
+            rope_dim=rope_dim, T=end_pos // ratio, topk=self.index_topk, ratio=ratio,
+            causal=start_pos == 0, offset=offset, pos0=0)
 
 
 def get_inputs():

@@ -9,6 +9,8 @@ These are the B200 counterparts of the reference's torch extension ops
   (indexer_torch.cpp:100-268), fused behind one call
 * ``indexer_scores`` / ``topk_rows`` expose the two indexer stages separately.
 * ``dsa`` runs the indexer's int32 top-k straight into ``sparse_attn`` in one call.
+* ``proj_rope``: the indexer's projections (``wq_b`` + RoPE, ``weights_proj`` x scale)
+  on the tensor cores, the producer of ``indexer_topk``'s inputs.
 * ``quant_fp8_rows`` / ``indexer_topk_fp8`` / ``indexer_scores_fp8``: the FP8 indexer
   (``ModelArgs.dtype = "fp8"``), which the reference declares but does not implement.
 
@@ -245,6 +247,44 @@ def dsa(q_ix: torch.Tensor, k_ix: torch.Tensor, w: torch.Tensor, freqs: torch.Te
                            _ptr(out), _ptr(workspace), workspace.numel() * workspace.element_size(),
                            _stream(q_ix)), "ks_dsa")
     return out, idx_out
+
+
+def proj_rope(a: torch.Tensor, w: torch.Tensor, head_dim: int = 0, rope_dim: int = 0,
+              freqs: torch.Tensor | None = None, scale: float | None = None,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """``F.linear(a, w)`` (bf16, fp32 accumulation) on the tensor cores with the
+    indexer's follow-up arithmetic fused into the epilogue: with ``rope_dim`` the
+    last ``rope_dim`` of every ``head_dim`` output columns are rotated by
+    ``freqs[s]`` ([S, rope_dim/2, 2] fp32, row s of the sequence dim, i.e. dim -2
+    of ``a``), as baseline/indexer.py:114-129,172; with ``scale`` the bf16
+    result is multiplied by it and rounded again (baseline/indexer.py:173-175).
+    a bf16 [..., K], w bf16 [N, K] -> bf16 [..., N]."""
+    if a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise RuntimeError("proj_rope: a and w must be bfloat16")
+    if a.dim() < 1 or w.dim() != 2 or a.shape[-1] != w.shape[1]:
+        raise RuntimeError("proj_rope: expected a [..., K] and w [N, K]")
+    if freqs is not None and freqs.dtype != torch.float32:
+        raise RuntimeError("proj_rope: freqs must be float32 [S, rope_dim/2, 2]")
+    if rope_dim and freqs is None:
+        raise RuntimeError("proj_rope: rope_dim needs freqs")
+    ts = [a, w] + ([freqs] if freqs is not None else [])
+    _require_cuda("proj_rope", *ts)
+    N, K = w.shape
+    M = a.numel() // K
+    S = a.shape[-2] if a.dim() >= 2 else 1
+    if rope_dim and freqs.shape[0] < S:
+        raise RuntimeError("proj_rope: freqs has fewer rows than the sequence")
+    shape = tuple(a.shape[:-1]) + (N,)
+    if out is None:
+        out = torch.empty(shape, dtype=torch.bfloat16, device=a.device)
+    else:
+        _check_out("proj_rope", out, shape, torch.bfloat16, a.device)
+    with torch.cuda.device(a.device):
+        check(lib().ks_proj_rope(_ptr(a), _ptr(w), _ptr(out), M, N, K, int(head_dim),
+                                 int(rope_dim), _ptr(freqs), S,
+                                 float(scale) if scale is not None else 1.0,
+                                 int(scale is not None), _stream(a)), "ks_proj_rope")
+    return out
 
 
 _FP8 = (torch.float8_e4m3fn, torch.uint8)

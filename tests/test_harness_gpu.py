@@ -49,20 +49,35 @@ def _tie_order_ascending(vals: torch.Tensor, idx: torch.Tensor) -> float:
     return (same & asc).sum().item() / n if n else 1.0
 
 
-def test_indexer_under_the_harness(cuda_ok):
+@pytest.mark.parametrize("fused", [True, False])
+def test_indexer_under_the_harness(cuda_ok, fused):
+    """fused: the drop-in's projections run in ops.proj_rope (the default);
+    otherwise in torch, exactly as v0 computes them."""
     from kernelswift_b200 import ops
 
-    v0, o0, v1, o1, inputs = Hn.harness_run("indexer", DEV)
-    problem = Hn.compare(o0, o1)
+    v0, o0, v1, _, inputs = Hn.harness_run("indexer", DEV)
     x, qr, start_pos, offset = inputs
+    v1.fused_projections = fused
+    Hn.set_seed(42)
+    with torch.no_grad():
+        o1 = v1(*Hn.clone_value(inputs))
+    problem = Hn.compare(o0, o1)
     sc0 = v0.last_scores                                  # v0's masked bf16 scores [B, S, T]
     B, S, T = sc0.shape
-    # the kernel's own scores on the same projected, un-rotated queries
-    with torch.no_grad():
-        q = v1.wq_b(qr).unflatten(-1, (v1.n_local_heads, v1.head_dim)).contiguous()
-        w = (v1.weights_proj(x) * (v1.softmax_scale * v1.n_heads ** -0.5)).contiguous()
+    # the kernel's own scores on the queries and weights this mode produces
     fr = torch.view_as_real(v1.freqs_cis[:S]).float().contiguous()
-    sc1 = ops.indexer_scores(q, v1.kv_cache[:B], w, fr, v1.rope_head_dim, T, v1.compress_ratio)
+    scale = v1.softmax_scale * v1.n_heads ** -0.5
+    with torch.no_grad():
+        if fused:
+            q = ops.proj_rope(qr, v1.wq_b.weight, v1.head_dim, v1.rope_head_dim, fr)
+            w = ops.proj_rope(x, v1.weights_proj.weight, scale=scale)
+            rd, f = 0, None
+        else:
+            q = v1.wq_b(qr)
+            w = v1.weights_proj(x) * scale
+            rd, f = v1.rope_head_dim, fr
+    q = q.unflatten(-1, (v1.n_local_heads, v1.head_dim)).contiguous()
+    sc1 = ops.indexer_scores(q, v1.kv_cache[:B], w.contiguous(), f, rd, T, v1.compress_ratio)
     ops.device_status()
     sc1 = sc1[..., :T]
     lim = (torch.arange(1, S + 1, device=DEV) // v1.compress_ratio)[None, :, None]
@@ -79,10 +94,11 @@ def test_indexer_under_the_harness(cuda_ok):
     real = differ & ~tie_rows & ~flip_rows
     t_vals, t_idx = sc0.topk(min(v1.index_topk, T), dim=-1)
     asc = _tie_order_ascending(t_vals, t_idx)
-    print(f"\nindexer under the harness: torch.equal {'passes' if problem is None else 'fails'}"
-          f" ({problem}); rows differing {differ.sum().item()} of {B * S}: tie order only "
-          f"{tie_rows.sum().item()}, rows with a score flip {(differ & flip_rows).sum().item()}, "
-          f"other {real.sum().item()}; score flips {((sc1 != sc0) & valid).float().mean().item():.2e}"
-          f" of valid scores; CUDA torch.topk tie order ascending for {asc:.4f} of tied pairs")
+    print(f"\nindexer under the harness (projections {'fused' if fused else 'torch'}): torch.equal "
+          f"{'passes' if problem is None else 'fails'} ({problem}); rows differing "
+          f"{differ.sum().item()} of {B * S}: tie order only {tie_rows.sum().item()}, rows with a "
+          f"score flip {(differ & flip_rows).sum().item()}, other {real.sum().item()}; score "
+          f"flips {((sc1 != sc0) & valid).float().mean().item():.2e} of valid scores; CUDA "
+          f"torch.topk tie order ascending for {asc:.4f} of tied pairs")
     assert real.sum().item() == 0
     assert ((sc1 != sc0) & valid).float().mean().item() <= 1e-3
