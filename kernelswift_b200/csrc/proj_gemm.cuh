@@ -143,7 +143,6 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lanes [32 quarter, +32)
     const int row_in_tile = quarter * 32 + lane;
-    const int half_rd = p.rd / 2;
     const int rope0 = p.hd - p.rd;  // first rotated column of a head
     uint32_t ac = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++ac) {

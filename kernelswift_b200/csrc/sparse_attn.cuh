@@ -302,24 +302,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       }
     }
   } else if (warp == SA_MMA_WARP || warp == SA_MMA_WARP + 1) {
-    if (lane == 0 && cta == 0) {
+    if (cta == 0) {
       // ---------------------------------------------------------- MMA issuers (leader CTA)
-      // Two threads in two warps: warp 8 issues the QK chunks, warp 9 the V
-      // chunks, each in ring order.  One thread alone keeps the tensor cores
-      // about half busy (its barrier waits and commits cannot overlap its own
-      // MMAs); two interleave.  Each stream has its own "full" barrier per slot,
-      // so a barrier phase is never awaited while an earlier phase of the other
-      // stream in that slot is still open.  The waits are compiled in (a call
-      // here costs more than the four MMAs of a chunk) and CTA-scoped: the data
-      // they publish is read by the tensor cores, not by this thread.
+      // Two warps: warp 8 issues the QK chunks, warp 9 the V chunks, each in
+      // ring order.  One issuing thread alone keeps the tensor cores about half
+      // busy (its barrier waits and commits cannot overlap its own MMAs); two
+      // interleave.  Each stream has its own "full" barrier per slot, so a barrier
+      // phase is never awaited while an earlier phase of the other stream in that
+      // slot is still open.  The whole warp runs the loop: every lane waits on the
+      // same barrier phase and computes the same (warp-uniform) descriptors, and
+      // one elected lane (always the same one: the commits track the MMAs of the
+      // thread that issued them) issues the MMAs and commits.  The waits are
+      // compiled in (a call here costs more than the four MMAs of a chunk) and
+      // CTA-scoped: the data they publish is read by the tensor cores, not by
+      // this warp.
       const bool v_issuer = warp != SA_MMA_WARP;
-      bool ok = mbar_wait(&sh->q_full, 0, wc) && mbar_wait(&sh->peer_q, 0, wc, true);
+      const bool leader = elect_one();
+      bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->q_full, 0, wc) &&
+                                            mbar_wait(&sh->peer_q, 0, wc, true));
       // Descriptors are built once; a byte offset o moves the start address field by o / 16.
       const uint64_t rd0 = sdesc_sw128(smem_u32(smem + p.r_off), v_issuer ? SA_VSEG : 16, 1024);
       uint32_t ph = 0;  // bit k: parity of the next phase of slot k's full barrier for this stream
       // Ring position (rn) and slot (rs = rn mod n_slots) of this stream's next
-      // chunk, advanced incrementally: this thread's per-chunk work is a short
-      // dependent chain, so it carries no division.  Ring order S(0) | S(1) V(0) |
+      // chunk, advanced incrementally: the per-chunk work is a short dependent
+      // chain, so it carries no division.  Ring order S(0) | S(1) V(0) |
       // S(2) V(1) | ... | V(nblk-1): the QK stream starts at 0 and skips V(j-2)
       // before S(j), j >= 2; the V stream starts after S(1) and skips S(j+2) after V(j).
       const int ns = p.n_slots;
@@ -339,6 +345,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         const uint32_t q0 = (ph >> s0) & 1u;
         bool r0 = mbar_poll(smem_u32(&fulls[s0]), q0);
         if (!r0) r0 = mbar_wait_inl(&fulls[s0], q0, wc);
+        r0 = __all_sync(0xFFFFFFFFu, r0);
         ph ^= 1u << s0;
         tc_fence_after();
         return r0;
@@ -351,7 +358,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         for (int j = 0; ok && j < p.nblk; ++j) {
           // S buffer j % 2 was last read by softmax(j - 2)
           wc.tag = 2000 + j;
-          if (j >= 2 && !(ok = mbar_wait_inl(&sh->s_free[j & 1], ((j - 2) >> 1) & 1, wc))) break;
+          if (j >= 2 && !(ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->s_free[j & 1], ((j - 2) >> 1) & 1, wc)))) break;
           const uint32_t d_s = tmem + (j & 1) * SA_SCOLS;
           if (j >= 2) adv(SA_NKC);
           for (int d = 0; d < nkb; ++d) {
@@ -361,16 +368,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
             adv(1);
             const uint32_t blo = rlo + (uint32_t)(slh * (SA_SLOT >> 4));
             const uint32_t alo = qlo + (uint32_t)(d * 512);
+            if (leader) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_cg2_w(d_s, alo + kk * 2, qhi, blo + kk * 2, rhi, idesc_s, (d > 0 || kk > 0) ? 1u : 0u);
-            umma_commit_cg2(&sh->empty[slh], 3);
+              for (int kk = 0; kk < 4; ++kk)
+                umma_cg2_w(d_s, alo + kk * 2, qhi, blo + kk * 2, rhi, idesc_s, (d > 0 || kk > 0) ? 1u : 0u);
+              umma_commit_cg2(&sh->empty[slh], 3);
+            }
+            __syncwarp();
             KS_SA_TRACE(12, n);
           }
           if (!ok) break;
-          umma_commit_cg2(&sh->acc_full[j & 1], 3);
+          if (leader) umma_commit_cg2(&sh->acc_full[j & 1], 3);
+          __syncwarp();
         }
-        umma_commit_cg2(&sh->drain_s, 1);
+        if (leader) umma_commit_cg2(&sh->drain_s, 1);
+        __syncwarp();
         mbar_wait(&sh->drain_s, 0, wc, false, true);
       } else {
         const uint64_t pd0 = sdesc_sw128(smem_u32(ps), 16, 1024);
@@ -383,7 +395,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         for (int j = 0; ok && j < p.nblk; ++j) {
           // P(j) written (and O rescaled) by the softmax
           wc.tag = 1000 + j;
-          if (!(ok = mbar_wait_inl(&sh->p_full[j & 1], (j >> 1) & 1, wc))) break;
+          if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->p_full[j & 1], (j >> 1) & 1, wc)))) break;
           KS_SA_TRACE(8, j);
           for (int sp = 0; sp < SA_NKC; sp += 2) {
 #pragma unroll
@@ -395,28 +407,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
               adv(1);
               const uint32_t boff = (uint32_t)(slh * (SA_SLOT >> 4));
               const uint32_t alo = plo + (uint32_t)((j & 1) * (SA_PBYTES >> 4) + (sub >> 1) * 512 + (sub & 1) * 4);
+              if (leader) {
 #pragma unroll
-              for (int i = 0; i < 2; ++i) {
-                if (i == 1 && npv < 2) break;
-                // instruction i: N = pv_n[i]; its columns start at segment 2 i (pv_n[0] = 256 when there are two)
-                const uint32_t ocol = tmem + SA_OCOL + (i ? pvn0 / 2 : 0);
-                const uint32_t blo = rlo + boff + (uint32_t)(i ? (pvn0 / 128) * (SA_VSEG >> 4) : 0);
+                for (int i = 0; i < 2; ++i) {
+                  if (i == 1 && npv < 2) break;
+                  // instruction i: N = pv_n[i]; its columns start at segment 2 i (pv_n[0] = 256 when there are two)
+                  const uint32_t ocol = tmem + SA_OCOL + (i ? pvn0 / 2 : 0);
+                  const uint32_t blo = rlo + boff + (uint32_t)(i ? (pvn0 / 128) * (SA_VSEG >> 4) : 0);
 #pragma unroll
-                for (int kk = 0; kk < SA_KC / 16; ++kk)
-                  umma_cg2_w(ocol, alo + kk * 2, phi, blo + kk * 128, rhi, i ? idesc_pv1 : idesc_pv0,
-                             (j > 0 || sub > 0 || kk > 0) ? 1u : 0u);
+                  for (int kk = 0; kk < SA_KC / 16; ++kk)
+                    umma_cg2_w(ocol, alo + kk * 2, phi, blo + kk * 128, rhi, i ? idesc_pv1 : idesc_pv0,
+                               (j > 0 || sub > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit_cg2(&sh->empty[slh], 3);
               }
-              umma_commit_cg2(&sh->empty[slh], 3);
+              __syncwarp();
               KS_SA_TRACE(12, n);
             }
             if (!ok) break;
           }
           if (!ok) break;
-          umma_commit_cg2(&sh->p_free[j & 1], 3);
+          if (leader) umma_commit_cg2(&sh->p_free[j & 1], 3);
+          __syncwarp();
           if (j + 2 < p.nblk) adv(nkb);
         }
-        if (ok) umma_commit_cg2(&sh->o_full, 3);
-        umma_commit_cg2(&sh->drain_v, 1);
+        if (ok && leader) umma_commit_cg2(&sh->o_full, 3);
+        if (leader) umma_commit_cg2(&sh->drain_v, 1);
+        __syncwarp();
         mbar_wait(&sh->drain_v, 0, wc, false, true);
       }
     } else if (lane == 0 && warp == SA_MMA_WARP) {
