@@ -445,24 +445,27 @@ class SparseAttnOp(SingleOp):
 
 
 class IndexerOp(SingleOp):
-    """C3: q (1, 4096, 64, 128) before RoPE, keys (1, 4096, 128), rope 64, top-2048, causal."""
+    """C3: q (1, 4096, 64, 128) before RoPE, keys (1, 4096, 128), rope 64, top-2048, causal.
+    With `seq` set (C5's indexer stage: B=2, seq 32768), `tokens` selects the LAST
+    `tokens` rows of the sequence (the longest causal rows) over all `seq` keys."""
 
-    def __init__(self, rank, world, device, tokens=None):
+    def __init__(self, rank, world, device, tokens=None, B=1, seq=None):
         super().__init__(rank, world, device, tokens)
-        self.B, self.H, self.D, self.rd, self.k = 1, 64, 128, 64, 2048
-        self.S = tokens or 4096
-        self.T = self.S
+        self.B, self.H, self.D, self.rd, self.k = B, 64, 128, 64, 2048
+        self.T = seq or tokens or 4096
+        self.S = tokens or self.T
+        self.row0 = self.T - self.S  # position of the first row
         self.units = self.B * self.S
         self.desc = (f"Indexer bf16 q ({self.B}, {self.S}, {self.H}, {self.D}) before RoPE, keys "
                      f"({self.B}, {self.T}, {self.D}), RoPE on the last {self.rd} dims, causal, "
-                     f"top-{self.k} int64")
+                     f"top-{self.k} int64" + (f", rows {self.row0}..{self.T - 1}" if self.row0 else ""))
         self.l2 = "inputs larger than L2"
         if device is None:
             return
         import torch
         from kernelswift_b200 import ops, shard
 
-        self.ranges = shard.zigzag(self.S, world, rank)
+        self.ranges = [(a + self.row0, b + self.row0) for a, b in shard.zigzag(self.S, world, rank)]
         self.launches = 2 * len(self.ranges)
         g = torch.Generator(device=device).manual_seed(13 + rank)
         self.kx = torch.randn(self.B, self.T, self.D, device=device, generator=g).bfloat16()
@@ -472,7 +475,8 @@ class IndexerOp(SingleOp):
             self.w.append((torch.rand(self.B, b - a, self.H, device=device, generator=g) *
                            (self.D ** -0.5 * self.H ** -0.5)).bfloat16())
             self.fr.append(_freqs(b - a, self.rd, a).to(device))
-            self.out.append(torch.empty(self.B, b - a, self.k, dtype=torch.int64, device=device))
+            self.out.append(torch.empty(self.B, b - a, min(self.k, self.T), dtype=torch.int64,
+                                        device=device))
         self.ws = torch.empty(max(ops.indexer_workspace_size(self.B, b - a, self.T) for a, b in self.ranges),
                               dtype=torch.uint8, device=device)
         self.inputs, self.outputs = self.q + self.w, self.out
@@ -496,14 +500,14 @@ class IndexerOp(SingleOp):
         n = budget_rows[0]
         kx = O.f32_to_bf16(rng.standard_normal((1, self.T, self.D)).astype(np.float32))
         t_ix = 0.0
-        for s in np.linspace(0, self.S - 1, n).astype(int):
+        for s in np.linspace(self.row0, self.T - 1, n).astype(int):
             q = O.f32_to_bf16(rng.standard_normal((1, 1, self.H, self.D)).astype(np.float32))
             w = O.f32_to_bf16(rng.uniform(0, 0.01, (1, 1, self.H)).astype(np.float32))
             t0 = time.perf_counter()
             O.indexer_forward(q, kx[:, : s + 1], w, _freqs(1, self.rd, int(s)).numpy(), self.rd,
                               self.k, 1, 0, 0, s0=int(s))
             t_ix += time.perf_counter() - t0
-        return n / t_ix, f"{n} rows spread over positions 0..{self.S - 1}, time per row"
+        return n / t_ix, f"{n} rows spread over positions {self.row0}..{self.T - 1}, time per row"
 
 
 class CopyPipeline:
@@ -665,6 +669,7 @@ WORKLOADS = {
     "c2": lambda r, w, d, tokens=None: SparseAttnOp(r, w, d, tokens, "c2"),
     "c3": lambda r, w, d, tokens=None: IndexerOp(r, w, d, tokens),
     "c4": lambda r, w, d, tokens=None: SparseAttnOp(r, w, d, tokens, "c4"),
+    "c5_indexer": lambda r, w, d, tokens=None: IndexerOp(r, w, d, tokens, B=2, seq=32768),
     "c5_sinkhorn": lambda r, w, d, tokens=None: SinkhornOp(r, w, d, tokens, (2, 32768, 8, 8)),
 }
 
