@@ -5,6 +5,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstdlib>
 #include <mutex>
 #include <string>
@@ -16,6 +17,7 @@
 #include "quant_fp8.cuh"
 #include "sinkhorn.cuh"
 #include "sparse_attn.cuh"
+#include "sparse_attn_small.cuh"
 #include "topk.cuh"
 
 namespace ks {
@@ -331,6 +333,47 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
   if (B * M * H >= (1ll << 31) || B * N >= (1ll << 31) || 2 * B * M >= (1ll << 31))
     return fail(KS_ERR_UNSUPPORTED, "sparse_attn: too many rows");
   if (M == 0) return KS_OK;
+  // Few heads and short index rows: one CTA per token, keys as the MMA's M
+  // dimension (sparse_attn_small.cuh).
+  {
+    const int hn = H <= 16 ? 16 : H <= 32 ? 32 : H <= 64 ? 64 : 0;
+    const int64_t k_pad = round_up(K, 128), nt = k_pad / 128;
+    const int dv_tiles = (int)((dv + 127) / 128);
+    const int nkb = (int)std::max<int64_t>(D / 64, dv_begin / 64 + 2 * dv_tiles);
+    const size_t kg = (size_t)nt * nkb * 16384, qb = (size_t)nkb * hn * 128,
+                 pb = (size_t)(k_pad / 64) * hn * 128;
+    const size_t smem = 1024 + SAS_HDR + kg + qb + pb;
+    int cols = (int)(nt * hn + dv_tiles * hn);
+    int tcols = 32;
+    while (tcols < cols) tcols <<= 1;
+    if (hn > 0 && K <= SAS_MAX_K && dv <= 256 && smem <= 232448 && tcols <= 512) {
+      SaSmallParams sp{};
+      sp.q = static_cast<const uint16_t*>(q);
+      sp.idx = idx;
+      sp.kv = static_cast<const uint16_t*>(kv);
+      sp.sink = sink;
+      sp.out = static_cast<uint16_t*>(out);
+      sp.B = (int)B; sp.M = (int)M; sp.H = (int)H; sp.D = (int)D; sp.N = (int)N; sp.K = (int)K;
+      sp.dv_begin = (int)dv_begin; sp.dv = (int)dv;
+      sp.nt = (int)nt; sp.nkb = nkb; sp.dv_tiles = dv_tiles;
+      sp.kg_off = SAS_HDR;
+      sp.q_off = (uint32_t)(SAS_HDR + kg);
+      sp.p_off = (uint32_t)(SAS_HDR + kg + qb);
+      sp.tmem_cols = (uint32_t)tcols;
+      sp.scale_log2 = scale * 1.4426950408889634f;
+      sp.status = dev->status;
+      sp.budget_ns = wait_budget_ns();
+      const void* fn = hn == 16 ? reinterpret_cast<const void*>(sparse_attn_small_kernel<16>)
+                     : hn == 32 ? reinterpret_cast<const void*>(sparse_attn_small_kernel<32>)
+                                : reinterpret_cast<const void*>(sparse_attn_small_kernel<64>);
+      if (int rc = smem_optin(dev, fn, "cudaFuncSetAttribute(sparse_attn_small)")) return rc;
+      const unsigned grid = (unsigned)(B * M);
+      if (hn == 16) sparse_attn_small_kernel<16><<<grid, SAS_THREADS, smem, st>>>(sp);
+      else if (hn == 32) sparse_attn_small_kernel<32><<<grid, SAS_THREADS, smem, st>>>(sp);
+      else sparse_attn_small_kernel<64><<<grid, SAS_THREADS, smem, st>>>(sp);
+      return launch_check("sparse_attn_small_kernel launch");
+    }
+  }
   SaParams p{};
   p.idx = idx;
   p.kv = static_cast<const uint16_t*>(kv);

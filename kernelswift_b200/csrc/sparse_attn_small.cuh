@@ -1,0 +1,295 @@
+// Top-k sparse attention for few heads (H <= 64) and short index rows (K <= 512):
+// one CTA per query token, keys as the MMA's M dimension.
+//
+// Semantics are those of sparse_attn_kernel (baseline/sparse_attention.py:5-42).
+// With H = 16 (C2) or the reference's own default (H = 64, K = 16) the head
+// count fills only a fraction of an M = 128 tile, so the product is transposed:
+//   S^T[keys, heads] = K_g[keys, D] . Q^T          M = 128 keys, N = Hn (H rounded up)
+//   O^T[dims, heads] = V^T[dims, keys] . P^T        M = 128 output dims, N = Hn
+// The gathered rows are the A operand of both products: K-major (rows = keys) for
+// QK and, read as MN-major (dims contiguous), V^T for PV, so nothing is gathered
+// twice.  All K keys stay resident (K_pad x D_alloc x 2 bytes of shared memory),
+// so the softmax sees every score at once: one exact max and sum per head, no
+// rescaling.  P is rounded to bf16 for the PV product and the normalisation is
+// applied in fp32 at the end, as in sparse_attn_kernel.
+//
+// One CTA of 256 threads: all 8 warps gather (cp.async, 16 bytes per copy, zeros
+// for masked keys); warp 4 issues the MMAs (one elected lane); warps 0-3 (TMEM lane
+// quarters) run the softmax over the S^T columns and the epilogue over O^T.
+#pragma once
+#include "ks_device.cuh"
+
+namespace ks {
+
+constexpr int SAS_THREADS = 256;
+constexpr int SAS_MAX_K = 512;
+constexpr int SAS_HDR = 2048;
+
+struct SaSmallParams {
+  const uint16_t* q;    // bf16 [B, M, H, D]
+  const int32_t* idx;   // [B, M, K]
+  const uint16_t* kv;   // bf16 [B, N, D]
+  const float* sink;    // [H]
+  uint16_t* out;        // bf16 [B, M, H, dv]
+  int32_t B, M, H, D, N, K, dv_begin, dv;
+  int32_t nt;           // 128-key tiles (K_pad / 128)
+  int32_t nkb;          // 64-dim chunks held per key row (covers D and the PV columns)
+  int32_t dv_tiles;     // 128-row M tiles of O^T
+  uint32_t kg_off, q_off, p_off;  // shared-memory regions (bytes from the aligned base)
+  uint32_t tmem_cols;
+  float scale_log2;
+  int* status;
+  uint64_t budget_ns;
+};
+
+struct SaSmallShared {
+  uint64_t mma_bar;
+  uint32_t tmem_base;
+  int abort;
+  int oob;
+  float red[4][64];     // per-warp partial max / sum per head
+  float head_m[64];     // max per head (base-2 scaled), sink included
+  float head_inv[64];   // 1 / denominator per head
+};
+static_assert(sizeof(SaSmallShared) <= SAS_HDR, "SaSmallShared exceeds its header");
+
+template <int HN>
+__global__ void __launch_bounds__(SAS_THREADS)
+    sparse_attn_small_kernel(SaSmallParams p) {
+  extern __shared__ uint8_t sas_raw[];
+  const uint32_t raw = smem_u32(sas_raw);
+  uint8_t* smem = sas_raw + (((raw + 1023u) & ~1023u) - raw);
+  SaSmallShared* sh = reinterpret_cast<SaSmallShared*>(smem);
+  uint8_t* kg = smem + p.kg_off;  // [nt][nkb][128 keys x 128 B], 128-byte swizzle
+  uint8_t* qs = smem + p.q_off;   // [nkb][HN rows x 128 B]
+  uint8_t* ps = smem + p.p_off;   // P^T [K_pad / 64][HN rows x 128 B] (K-major: keys contiguous)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t token = blockIdx.x;
+  const int b = (int)(token / p.M);
+  const int K_pad = p.nt * 128;
+  WaitCtx wc{&sh->abort, p.status, p.budget_ns};
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sh->mma_bar, 1);
+    sh->abort = 0;
+    sh->oob = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc<1>(&sh->tmem_base, p.tmem_cols);
+    tmem_relinquish<1>();
+  }
+
+  // ---------------------------------------------------------------- gathers
+  // Key rows: piece c (16 bytes) of key k lands in tile k / 128, chunk c / 8, row
+  // k % 128, 16-byte unit (c % 8) ^ (k % 8).  Masked keys (negative, >= N, or past
+  // K) are zero-filled; the D columns past D (when nkb covers more) too.
+  const int32_t* ip = p.idx + token * p.K;
+  const uint16_t* kvb = p.kv + (int64_t)b * p.N * p.D;
+  {
+    const int pieces_per_row = p.nkb * 8;
+    const int total = K_pad * pieces_per_row;
+    for (int e = threadIdx.x; e < total; e += SAS_THREADS) {
+      const int k = e / pieces_per_row, c = e % pieces_per_row;
+      const int32_t v = k < p.K ? __ldg(ip + k) : -1;
+      const bool ok = v >= 0 && v < p.N && c * 8 < p.D;
+      if (k < p.K && v >= p.N) sh->oob = 1;
+      uint8_t* dst = kg + ((k >> 7) * p.nkb + (c >> 3)) * 16384 + (k & 127) * 128 +
+                     (((c & 7) ^ (k & 7)) << 4);
+      cp_async16(dst, ok ? kvb + (int64_t)v * p.D + c * 8 : kvb, ok ? 16u : 0u);
+    }
+    // the query rows (heads) h < H of this token, zeros for the padding rows
+    const uint16_t* qt = p.q + token * (int64_t)p.H * p.D;
+    const int qpieces = HN * p.nkb * 8;
+    for (int e = threadIdx.x; e < qpieces; e += SAS_THREADS) {
+      const int h = e / (p.nkb * 8), c = e % (p.nkb * 8);
+      const bool ok = h < p.H && c * 8 < p.D;
+      uint8_t* dst = qs + (c >> 3) * (HN * 128) + h * 128 + (((c & 7) ^ (h & 7)) << 4);
+      cp_async16(dst, ok ? qt + (int64_t)h * p.D + c * 8 : qt, ok ? 16u : 0u);
+    }
+    cp_async_wait_all();
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+  const uint32_t s_col = 0, o_col = (uint32_t)(p.nt * HN);
+
+  // ---------------------------------------------------------------- QK^T
+  if (warp == 4) {
+    const bool leader = elect_one();
+    if (leader) {
+      const uint32_t idesc = idesc_bf16_f32(128, HN, false, false);
+      const int ksteps = (p.D + 15) / 16;
+      for (int t = 0; t < p.nt; ++t)
+        for (int ks = 0; ks < ksteps; ++ks) {
+          const uint32_t a = smem_u32(kg + (t * p.nkb + (ks >> 2)) * 16384) + (ks & 3) * 32;
+          const uint32_t bq = smem_u32(qs + (ks >> 2) * (HN * 128)) + (ks & 3) * 32;
+          umma_bf16_ss(tmem + s_col + t * HN, sdesc_sw128(a, 16, 1024), sdesc_sw128(bq, 16, 1024),
+                       idesc, ks > 0 ? 1u : 0u);
+        }
+      umma_commit(&sh->mma_bar);
+    }
+    __syncwarp();
+  }
+
+  // ---------------------------------------------------------------- softmax (warps 0-3)
+  // Thread = key (k = 32 warp + lane within each 128-key tile).  Heads go in
+  // groups of 16 TMEM columns; each pass re-reads S^T from TMEM, so registers do
+  // not grow with H or K.  Max and sum per head are reduced over the warp by a
+  // shuffle butterfly and over the four warps through shared memory.
+  if (warp < 4) {
+    const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->mma_bar, 0, wc));
+    uint32_t vmask = 0;  // bit t: this thread's key of tile t is valid
+    for (int t = 0; t < p.nt; ++t) {
+      const int k = t * 128 + warp * 32 + lane;
+      const int32_t v = k < p.K ? __ldg(ip + k) : -1;
+      vmask |= (uint32_t)(v >= 0 && v < p.N) << t;
+    }
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    if (ok) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int hg = 0; hg < HN; hg += 16) {
+        float mh[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) mh[i] = -INFINITY;
+        for (int t = 0; t < p.nt; ++t) {
+          uint32_t r[16];
+          tmem_ld16(tmem + s_col + t * HN + hg + lane_off, r);
+          tmem_wait_ld();
+          if ((vmask >> t) & 1u) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) mh[i] = fmaxf(mh[i], __uint_as_float(r[i]) * p.scale_log2);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) mh[i] = fmaxf(mh[i], __shfl_xor_sync(0xFFFFFFFFu, mh[i], o));
+        }
+        if (lane == 0) {  // (after the butterfly every lane holds the warp's maxima)
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sh->red[warp][hg + i] = mh[i];
+        }
+      }
+    }
+    named_bar_sync(1, 128);
+    if (ok && threadIdx.x < HN) {
+      const int h = threadIdx.x;
+      const float sink2 = h < p.H ? __ldg(p.sink + h) * 1.4426950408889634f : 0.f;
+      sh->head_m[h] = fmaxf(fmaxf(fmaxf(sh->red[0][h], sh->red[1][h]),
+                                  fmaxf(sh->red[2][h], sh->red[3][h])), sink2);
+    }
+    named_bar_sync(1, 128);
+    if (ok) {
+#pragma unroll 1
+      for (int hg = 0; hg < HN; hg += 16) {
+        float ls[16], hm[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          ls[i] = 0.f;
+          hm[i] = sh->head_m[hg + i];
+        }
+        for (int t = 0; t < p.nt; ++t) {
+          const int k = t * 128 + warp * 32 + lane;  // key of this thread in tile t
+          const bool valid = (vmask >> t) & 1u;
+          uint32_t r[16];
+          tmem_ld16(tmem + s_col + t * HN + hg + lane_off, r);
+          tmem_wait_ld();
+          const int kk = k & 63;
+          uint8_t* chunk = ps + (k >> 6) * (HN * 128);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int h = hg + i;
+            const float e = valid ? ex2f(fmaf(__uint_as_float(r[i]), p.scale_log2, -hm[i])) : 0.f;
+            ls[i] += e;
+            // P^T (K-major: row h holds the keys, 64 per 128-byte row): pairs of
+            // keys (even lane, odd lane) go out as one 32-bit store by the even lane
+            const float e_hi = __shfl_down_sync(0xFFFFFFFFu, e, 1);
+            if ((lane & 1) == 0)
+              *reinterpret_cast<uint32_t*>(chunk + h * 128 + (((kk >> 3) ^ (h & 7)) << 4) + (kk & 7) * 2) =
+                  cvt_bf16x2(e, e_hi);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) ls[i] += __shfl_xor_sync(0xFFFFFFFFu, ls[i], o);
+        }
+        if (lane == 0) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sh->red[warp][hg + i] = ls[i];
+        }
+      }
+      fence_proxy_async_smem();  // P^T is read by the tensor cores next
+    }
+    named_bar_sync(1, 128);
+    if (ok && threadIdx.x < HN) {
+      const int h = threadIdx.x;
+      const float sink2 = h < p.H ? __ldg(p.sink + h) * 1.4426950408889634f : 0.f;
+      const float den = (sh->red[0][h] + sh->red[1][h]) + (sh->red[2][h] + sh->red[3][h]) +
+                        ex2f(sink2 - sh->head_m[h]);
+      sh->head_inv[h] = 1.f / den;
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+
+  // ---------------------------------------------------------------- P V
+  if (warp == 4) {
+    const bool leader = elect_one();
+    if (leader) {
+      tc_fence_after();
+      const uint32_t idesc = idesc_bf16_f32(128, HN, true, false);
+      const int ksteps = K_pad / 16;
+      const int c0 = p.dv_begin / 64;
+      for (int m = 0; m < p.dv_tiles; ++m)
+        for (int ks = 0; ks < ksteps; ++ks) {
+          // A = V^T: dims [dv_begin + 128 m, +128) of keys [16 ks, +16), MN-major;
+          // its two 64-dim halves are chunks 16 KB apart (LBO)
+          const int t = ks >> 3;
+          const uint32_t a = smem_u32(kg + (t * p.nkb + c0 + 2 * m) * 16384) + (ks & 7) * 2048;
+          const uint32_t bp = smem_u32(ps + (ks >> 2) * (HN * 128)) + (ks & 3) * 32;
+          umma_bf16_ss(tmem + o_col + m * HN, sdesc_sw128(a, 16384, 1024), sdesc_sw128(bp, 16, 1024),
+                       idesc, ks > 0 ? 1u : 0u);
+        }
+      umma_commit(&sh->mma_bar);
+    }
+    __syncwarp();
+  }
+
+  // ---------------------------------------------------------------- epilogue (warps 0-3)
+  // Thread = output dim (TMEM lane) of each 128-dim tile; out[token, h, dim] for h < H.
+  if (warp < 4) {
+    if (__all_sync(0xFFFFFFFFu, mbar_wait(&sh->mma_bar, 1, wc))) {
+      tc_fence_after();
+      uint16_t* orow = p.out + token * (int64_t)p.H * p.dv;
+      for (int m = 0; m < p.dv_tiles; ++m) {
+        const int d = m * 128 + warp * 32 + lane;
+#pragma unroll
+        for (int c = 0; c < HN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(tmem + o_col + m * HN + c + ((uint32_t)(warp * 32) << 16), r);
+          tmem_wait_ld();
+          if (d < p.dv) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (c + i < p.H)
+                orow[(int64_t)(c + i) * p.dv + d] =
+                    __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[i]) * sh->head_inv[c + i]));
+          }
+        }
+      }
+    }
+    if (threadIdx.x == 0 && sh->oob) report_bounds(p.status, (int)token, p.N);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc<1>(tmem, p.tmem_cols);
+}
+
+}  // namespace ks
