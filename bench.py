@@ -334,7 +334,8 @@ class SinkhornOp(SingleOp):
         self.metric = "matrices/s"
         self.dtype = "f32"
         self.desc = f"Sinkhorn fp32 ({self.B}, {self.S}, {self.n}, {self.n}), 20 iterations, eps 1e-6"
-        self.l2 = "L2 flushed between steps (write of a 256 MB buffer, outside the timed op spans)"
+        self.l2 = ("L2 flushed before every call (256 MB write); op time = CUDA-graph replays of "
+                   "(flush + op) minus replays of the flush alone")
         self.flushes = True
         self.launches = 1
         if device is None:
@@ -353,13 +354,18 @@ class SinkhornOp(SingleOp):
         nbytes = 2 * self.x.numel() * 4
         return {"sinkhorn": nbytes}, "hbm"
 
-    def run(self, timers=None):
+    span_name = "sinkhorn"
+
+    def op(self):
         from kernelswift_b200 import ops
 
+        ops.sinkhorn(self.x, 20, 1e-6, out=self.out)
+
+    def run(self, timers=None):
         if timers is not None:
             self.flush.zero_()  # keep each step's input out of L2
         with _span(timers, "sinkhorn"):
-            ops.sinkhorn(self.x, 20, 1e-6, out=self.out)
+            self.op()
 
     def cpu_sample(self, budget_rows=None):
         from oracle import ks_oracle as O
@@ -387,7 +393,8 @@ class SparseAttnOp(SingleOp):
                      f"{self.N}, {self.D}) shared latent, top-{self.K} int32 indices "
                      f"({'randperm' if cfg == 'c2' else 'causal-valid'}), dv {self.dv}")
         self.l2 = ("inputs larger than L2" if cfg == "c4"
-                   else "L2 flushed between steps (write of a 256 MB buffer, outside the timed op spans)")
+                   else "L2 flushed before every call (256 MB write); op time = CUDA-graph replays "
+                        "of (flush + op) minus replays of the flush alone")
         self.flushes = cfg != "c4"
         self.launches = 1
         self.cfg = cfg
@@ -422,13 +429,18 @@ class SparseAttnOp(SingleOp):
             return None
         return SA_DRAM_BYTES_PER_TOKEN_MLA * self.B * self.rows
 
-    def run(self, timers=None):
+    span_name = "sparse_attn"
+
+    def op(self):
         from kernelswift_b200 import ops
 
+        ops.sparse_attn(self.q, self.kv, self.sink, self.idx, self.D ** -0.5, self.dv, out=self.out)
+
+    def run(self, timers=None):
         if timers is not None and self.cfg == "c2":
             self.flush.zero_()
         with _span(timers, "sparse_attn"):
-            ops.sparse_attn(self.q, self.kv, self.sink, self.idx, self.D ** -0.5, self.dv, out=self.out)
+            self.op()
 
     def cpu_sample(self, budget_rows=(8,)):
         from oracle import ks_oracle as O
@@ -701,6 +713,8 @@ def timed_region(wl, steps, world, local, device, barrier):
     import torch.distributed as dist
     from kernelswift_b200 import ops
 
+    if wl.flushes and hasattr(wl, "op"):
+        return timed_region_graphs(wl, steps, world, local, device, barrier)
     clocks = ClockSampler(local)
     clocks.start()
     timers = Timers()
@@ -729,6 +743,58 @@ def timed_region(wl, steps, world, local, device, barrier):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     return ms, spans, clk, ms_with_flush
+
+
+def timed_region_graphs(wl, steps, world, local, device, barrier):
+    """Device time of a single-op workload whose input fits in L2: two CUDA graphs,
+    (L2 flush + op) and (L2 flush alone), each replayed `steps` times under CUDA
+    events; the op's time per call is the difference of the two per-replay times.
+    The graphs take the host's launch work out of the measurement (for a kernel of
+    tens of microseconds an event span around a Python call would time the call),
+    and every timed call starts from a flushed L2."""
+    import torch
+    import torch.distributed as dist
+    from kernelswift_b200 import ops
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g_op, g_fl = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g_op, stream=side):
+            wl.flush.zero_()
+            wl.op()
+        with torch.cuda.graph(g_fl, stream=side):
+            wl.flush.zero_()
+    torch.cuda.current_stream().wait_stream(side)
+    for g in (g_op, g_fl):
+        for _ in range(3):
+            g.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ev[0].record()
+    for _ in range(steps):
+        g_op.replay()
+    ev[1].record()
+    ev[2].record()
+    for _ in range(steps):
+        g_fl.replay()
+    ev[3].record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ops.device_status()
+    t = torch.tensor([ev[0].elapsed_time(ev[1]) / steps, ev[2].elapsed_time(ev[3]) / steps],
+                     device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    with_flush, flush_only = float(t[0].item()), float(t[1].item())
+    ms = max(with_flush - flush_only, 1e-6)
+    del g_op, g_fl
+    return ms, {wl.span_name: ms}, clk, with_flush
 
 
 def roofline_of(wl, spans, peaks):

@@ -23,7 +23,7 @@ namespace ks {
 
 constexpr int SAS_THREADS = 256;
 constexpr int SAS_MAX_K = 512;
-constexpr int SAS_HDR = 2048;
+constexpr int SAS_HDR = 4096;
 
 struct SaSmallParams {
   const uint16_t* q;    // bf16 [B, M, H, D]
@@ -50,6 +50,7 @@ struct SaSmallShared {
   float red[4][64];     // per-warp partial max / sum per head
   float head_m[64];     // max per head (base-2 scaled), sink included
   float head_inv[64];   // 1 / denominator per head
+  int32_t idx[SAS_MAX_K];  // the token's index row, -1 past K
 };
 static_assert(sizeof(SaSmallShared) <= SAS_HDR, "SaSmallShared exceeds its header");
 
@@ -86,12 +87,15 @@ __global__ void __launch_bounds__(SAS_THREADS)
   // K) are zero-filled; the D columns past D (when nkb covers more) too.
   const int32_t* ip = p.idx + token * p.K;
   const uint16_t* kvb = p.kv + (int64_t)b * p.N * p.D;
+  // the index row first (one coalesced pass), so no row copy waits on an index load
+  for (int k = threadIdx.x; k < K_pad; k += SAS_THREADS) sh->idx[k] = k < p.K ? __ldg(ip + k) : -1;
+  __syncthreads();
   {
     const int pieces_per_row = p.nkb * 8;
     const int total = K_pad * pieces_per_row;
     for (int e = threadIdx.x; e < total; e += SAS_THREADS) {
       const int k = e / pieces_per_row, c = e % pieces_per_row;
-      const int32_t v = k < p.K ? __ldg(ip + k) : -1;
+      const int32_t v = sh->idx[k];
       const bool ok = v >= 0 && v < p.N && c * 8 < p.D;
       if (k < p.K && v >= p.N) sh->oob = 1;
       uint8_t* dst = kg + ((k >> 7) * p.nkb + (c >> 3)) * 16384 + (k & 127) * 128 +
@@ -143,8 +147,7 @@ __global__ void __launch_bounds__(SAS_THREADS)
     const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->mma_bar, 0, wc));
     uint32_t vmask = 0;  // bit t: this thread's key of tile t is valid
     for (int t = 0; t < p.nt; ++t) {
-      const int k = t * 128 + warp * 32 + lane;
-      const int32_t v = k < p.K ? __ldg(ip + k) : -1;
+      const int32_t v = sh->idx[t * 128 + warp * 32 + lane];
       vmask |= (uint32_t)(v >= 0 && v < p.N) << t;
     }
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
