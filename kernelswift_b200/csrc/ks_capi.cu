@@ -500,10 +500,9 @@ int ks_sinkhorn(const float* x, float* out, int64_t n_mats, int32_t n, int32_t r
   };
   if (blocks_reg > 0x7FFFFFFFll / 2) return fail(KS_ERR_UNSUPPORTED, "sinkhorn: too many matrices");
   // even n <= 8: two threads per matrix (SK_THREADS / 2 matrices per block)
-  auto launch_pair = [&](auto kern, int N) {
+  auto launch_pair = [&](auto kern, int) {
     const int64_t blocks = (n_mats + SK_THREADS / 2 - 1) / (SK_THREADS / 2);
-    const size_t smem = (size_t)(SK_THREADS / 2) * (N * N + 2) * 4;
-    kern<<<(unsigned)blocks, SK_THREADS, smem, st>>>(x, out, n_mats, repeat, eps);
+    kern<<<(unsigned)blocks, SK_THREADS, 0, st>>>(x, out, n_mats, repeat, eps);
   };
 
   switch (n) {

@@ -223,11 +223,23 @@ __global__ void __launch_bounds__(SK_THREADS)
 // column n/2 + k of one thread is local column k of its partner.  Row pass:
 // local.  Column pass: each thread forms the partial column sums of its rows;
 // one shuffle per column brings the partner's part of the columns this thread
-// updates, and one more returns the new v.  The reciprocal count per matrix is
-// that of the one-thread form.
-// Shared staging: a matrix's two row halves sit at word offsets 0 and n^2/2 + 1
-// (matrix stride n^2 + 2), which keeps a warp's per-thread reads on 32 distinct
-// banks.
+// updates, and one more returns the new v.
+// Reciprocals go in pairs (1/a = b r, 1/b = a r with r = 1/(a b)): the XU pipe
+// (rcp, ex2) runs 16 operations per clock per SM against 128 FMAs, and at C5's
+// size it bounded the kernel; the pairing trades half the reciprocals for three
+// multiplies.  The denominators are sums plus eps, far from the fp32 range ends,
+// so their products neither overflow nor underflow.
+// No shared-memory staging: each thread loads its own rows (a contiguous half
+// matrix, 16-byte loads when the half is a multiple of 16 bytes) and stores them
+// back the same way, so every warp starts as soon as its own loads land (the C5
+// batch is a single wave: a block-wide staging step made all its warps wait for
+// the slowest load).
+__device__ __forceinline__ void sk_rcp_pair(float a, float b, float& ra, float& rb) {
+  const float r = sk_rcp(a * b);
+  ra = b * r;
+  rb = a * r;
+}
+
 template <int N>
 __global__ void __launch_bounds__(SK_THREADS)
     sinkhorn_pair_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t n_mats,
@@ -237,37 +249,32 @@ __global__ void __launch_bounds__(SK_THREADS)
   constexpr int R = N / 2;         // rows per thread, and columns whose v it updates
   constexpr int C = N / 2;         // column pairs
   constexpr int HW = NN / 2;       // words per row half
-  constexpr int STRIDE = NN + 2;
-  constexpr int MPB = SK_THREADS / 2;
-  extern __shared__ float sk_smem[];
+  constexpr bool V4 = (HW % 4) == 0;
   const int tid = threadIdx.x;
-  const int ml = tid >> 1, h = tid & 1;
-  const int64_t mat0 = (int64_t)blockIdx.x * MPB;
-  const int nm = (int)min((int64_t)MPB, n_mats - mat0);
-  const float* src = x + mat0 * NN;
-  float* dst = out + mat0 * NN;
-  const int total = nm * NN;
-  auto slot = [](int e) -> int { return (e / NN) * STRIDE + e % NN + (e % NN >= HW ? 1 : 0); };
-
-  // coalesced load of the block's contiguous chunk into the staging layout
-  if (nm == MPB && (HW % 4) == 0) {
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-    for (int q = tid; q < total / 4; q += SK_THREADS) {
-      const float4 f = __ldcs(s4 + q);
-      float* d = sk_smem + slot(q * 4);  // a float4 never straddles a row half
-      d[0] = f.x; d[1] = f.y; d[2] = f.z; d[3] = f.w;
-    }
-  } else {
-    for (int e = tid; e < total; e += SK_THREADS) sk_smem[slot(e)] = __ldcs(src + e);
-  }
-  __syncthreads();
+  const int h = tid & 1;
+  const int64_t mat = (int64_t)blockIdx.x * (SK_THREADS / 2) + (tid >> 1);
+  const bool live = mat < n_mats;  // threads past the batch run the iteration (shuffles) on zeros
+  const float* src = x + (live ? mat : 0) * NN + h * HW;
+  float* dst = out + mat * NN + h * HW;
 
   {
-    // Every thread runs the iteration (the shuffles need all lanes); pairs past the
-    // batch's end work on unused staging slots that are never stored.
-    float* my = sk_smem + ml * STRIDE + h * (HW + 1);
-    const int rot = h * R;  // local column j = global column (j + rot) mod N
-    auto gcol = [&](int j) -> int { return j + rot < N ? j + rot : j + rot - N; };
+    // Every thread runs the iteration (the shuffles need all lanes).
+    float raw[HW];
+    if (live) {
+      if constexpr (V4) {
+#pragma unroll
+        for (int q = 0; q < HW / 4; ++q) {
+          const float4 f = __ldcs(reinterpret_cast<const float4*>(src) + q);
+          raw[4 * q] = f.x; raw[4 * q + 1] = f.y; raw[4 * q + 2] = f.z; raw[4 * q + 3] = f.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < HW; ++e) raw[e] = __ldcs(src + e);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < HW; ++e) raw[e] = 0.f;
+    }
     // K = softmax(x) + eps for this thread's rows, as (local) column pairs
     uint64_t kp[R][C];
     constexpr float kLog2e = 1.4426950408889634f;
@@ -275,7 +282,11 @@ __global__ void __launch_bounds__(SK_THREADS)
     for (int i = 0; i < R; ++i) {
       float r[N];
 #pragma unroll
-      for (int j = 0; j < N; ++j) r[j] = my[i * N + gcol(j)];
+      for (int j = 0; j < N; ++j) {
+        // global column (j + rot) mod N; rot is 0 or R, selected without indexing
+        const int j0 = j, j1 = j + R < N ? j + R : j + R - N;
+        r[j] = h ? raw[i * N + j1] : raw[i * N + j0];
+      }
       float m = r[0];
 #pragma unroll
       for (int j = 1; j < N; ++j) m = fmaxf(m, r[j]);
@@ -301,6 +312,7 @@ __global__ void __launch_bounds__(SK_THREADS)
         uint64_t vp[C];
 #pragma unroll
         for (int c = 0; c < C; ++c) vp[c] = sk_pack(v[2 * c], v[2 * c + 1]);
+        float d[R];
 #pragma unroll
         for (int i = 0; i < R; ++i) {
           uint64_t acc = sk_mul2(kp[i][0], vp[0]);
@@ -308,8 +320,16 @@ __global__ void __launch_bounds__(SK_THREADS)
           for (int c = 1; c < C; ++c) acc = sk_fma2(kp[i][c], vp[c], acc);
           float lo, hi;
           sk_unpack(acc, lo, hi);
-          u[i] = u[i] * sk_rcp(fmaf(u[i], lo + hi, eps));
+          d[i] = fmaf(u[i], lo + hi, eps);
         }
+#pragma unroll
+        for (int i = 0; i + 1 < R; i += 2) {
+          float r0, r1;
+          sk_rcp_pair(d[i], d[i + 1], r0, r1);
+          u[i] *= r0;
+          u[i + 1] *= r1;
+        }
+        if constexpr (R % 2) u[R - 1] *= sk_rcp(d[R - 1]);
       }
       // column pass: partial sums of this thread's rows, then v_j <- v_j / (v_j t_j + eps)
       uint64_t t[C];
@@ -329,40 +349,52 @@ __global__ void __launch_bounds__(SK_THREADS)
       for (int c = 0; c < C; ++c) sk_unpack(t[c], tf[2 * c], tf[2 * c + 1]);
       // this thread updates its local columns k < R; the partner sends its partial
       // sums of them (its local columns R + k) and gets back the new v
+      float d[R];
 #pragma unroll
       for (int k = 0; k < R; ++k) {
         const float theirs = __shfl_xor_sync(0xFFFFFFFFu, tf[R + k], 1);
-        v[k] = v[k] * sk_rcp(fmaf(v[k], tf[k] + theirs, eps));
+        d[k] = fmaf(v[k], tf[k] + theirs, eps);
       }
+#pragma unroll
+      for (int k = 0; k + 1 < R; k += 2) {
+        float r0, r1;
+        sk_rcp_pair(d[k], d[k + 1], r0, r1);
+        v[k] *= r0;
+        v[k + 1] *= r1;
+      }
+      if constexpr (R % 2) v[R - 1] *= sk_rcp(d[R - 1]);
 #pragma unroll
       for (int k = 0; k < R; ++k) v[R + k] = __shfl_xor_sync(0xFFFFFFFFu, v[k], 1);
     }
-    // x_ij = u_i K_ij v_j for this thread's rows
+    // x_ij = u_i K_ij v_j for this thread's rows, back in global column order
     uint64_t vp[C];
 #pragma unroll
     for (int c = 0; c < C; ++c) vp[c] = sk_pack(v[2 * c], v[2 * c + 1]);
+    float res[HW];
 #pragma unroll
     for (int i = 0; i < R; ++i) {
       const uint64_t ui = sk_pack(u[i], u[i]);
+      float loc[N];
 #pragma unroll
-      for (int c = 0; c < C; ++c) {
-        float lo, hi;
-        sk_unpack(sk_mul2(sk_mul2(kp[i][c], ui), vp[c]), lo, hi);
-        my[i * N + gcol(2 * c)] = lo;
-        my[i * N + gcol(2 * c + 1)] = hi;
+      for (int c = 0; c < C; ++c) sk_unpack(sk_mul2(sk_mul2(kp[i][c], ui), vp[c]), loc[2 * c], loc[2 * c + 1]);
+#pragma unroll
+      for (int g = 0; g < N; ++g) {
+        // global column g is local column (g - rot) mod N
+        const int l0 = g, l1 = g - R >= 0 ? g - R : g - R + N;
+        res[i * N + g] = h ? loc[l1] : loc[l0];
       }
     }
-  }
-  __syncthreads();
-
-  if (nm == MPB && (HW % 4) == 0) {
-    float4* d4 = reinterpret_cast<float4*>(dst);
-    for (int q = tid; q < total / 4; q += SK_THREADS) {
-      const float* sv = sk_smem + slot(q * 4);
-      __stcs(d4 + q, make_float4(sv[0], sv[1], sv[2], sv[3]));
+    if (live) {
+      if constexpr (V4) {
+#pragma unroll
+        for (int q = 0; q < HW / 4; ++q)
+          __stcs(reinterpret_cast<float4*>(dst) + q,
+                 make_float4(res[4 * q], res[4 * q + 1], res[4 * q + 2], res[4 * q + 3]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < HW; ++e) __stcs(dst + e, res[e]);
+      }
     }
-  } else {
-    for (int e = tid; e < total; e += SK_THREADS) __stcs(dst + e, sk_smem[slot(e)]);
   }
 }
 
