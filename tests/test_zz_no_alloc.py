@@ -29,8 +29,9 @@ def _inputs(B, S, T, H, D, rd, seed):
 
 
 def test_noalloc_matches_workspace_entry_point(cuda_ok):
-    """Two calls in a row with different shapes: the second must not see the
-    first call's leftovers in the shared scratch."""
+    """Calls in a row with different shapes: none may see an earlier call's
+    leftovers in the shared scratch (the last fills it exactly, after a call with
+    longer rows)."""
     from kernelswift_b200 import _lib, ops
 
     lib = _lib.lib()
@@ -38,6 +39,9 @@ def test_noalloc_matches_workspace_entry_point(cuda_ok):
     cases = [  # B, S, T, H, D, rd, k, ratio, causal, offset
         (1, 512, 512, 64, 128, 64, 256, 1, 1, 0),
         (2, 300, 77, 16, 64, 32, 128, 4, 1, 0),
+        (1, 130, 300, 32, 128, 64, 64, 1, 0, 9),       # not causal (decode-style), + offset
+        (1, 256, 16384, 64, 128, 64, 512, 1, 1, 0),    # longer rows than the next call
+        (1, 2048, 8192, 64, 128, 64, 2048, 1, 1, 0),   # score rows fill the 32 MiB exactly
     ]
     for seed, (B, S, T, H, D, rd, k, ratio, causal, offset) in enumerate(cases):
         q, kv, w, fr = _inputs(B, S, T, H, D, rd, seed)
