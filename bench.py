@@ -16,8 +16,9 @@ memory) through the public ops.  Inputs are seeded synthetic tensors of the
 configuration's shapes and distributions (no dataset is involved).
 
 ``--impl reference`` times the reference algorithm on the host cores instead
-(the CPU restatement in oracle/, all threads), on bounded row samples of the
-same workload, extrapolated to the full step; under torchrun only rank 0 runs.
+(the reference's torch forwards restated in oracle/ks_ref_torch.py, all threads:
+what baseline/*.py runs on a CPU), on bounded row samples of the same workload,
+extrapolated to the full step; under torchrun only rank 0 runs.
 """
 from __future__ import annotations
 
@@ -82,6 +83,15 @@ class Workload:
     def traffic(self, kernel):
         """DRAM bytes per step of `kernel` (scaled from an ncu capture), or None."""
         return None
+
+
+def _freqs_cis(S, rd, pos0=0):
+    """Complex RoPE factors of positions pos0.. (baseline/indexer.py get_init_inputs)."""
+    import torch
+
+    inv = 1.0 / (10000.0 ** (torch.arange(0, rd, 2, dtype=torch.float32) / rd))
+    ang = torch.outer(torch.arange(pos0, pos0 + S, dtype=torch.float32), inv)
+    return torch.polar(torch.ones_like(ang), ang)
 
 
 def _freqs(S, rd, pos0=0):
@@ -248,39 +258,46 @@ class DsaE2E(Workload):
                             "(sinkhorn)",
                 "l2": "inputs larger than L2 (126 MB) every step"}
 
-    # ---- CPU sample of the same workload (oracle restatement)
-    def cpu_sample(self, budget_rows=(8, 8, 8192)):
-        from oracle import ks_oracle as O
+    # ---- CPU sample of the same workload (the reference's torch forwards, host cores)
+    def cpu_sample(self, budget_rows=(16, 16, 8192)):
+        import torch
+        from oracle import ks_ref_torch as R
 
-        rng = np.random.default_rng(0)
+        torch.set_num_threads(os.cpu_count() or 1)
+        g = torch.Generator().manual_seed(0)
         n_ix, n_sa, n_sk = budget_rows
-        S = self.S
-        kx = O.f32_to_bf16(rng.standard_normal((1, S, self.D_ix)).astype(np.float32))
+        S, rows_per_chunk = self.S, 32
+        kx = torch.randn(1, S, self.D_ix, generator=g).bfloat16()
         t_ix = 0.0
-        # rows spread evenly over positions: mean causal cost of the sample ~ of the sequence
-        for s in np.linspace(0, S - 1, n_ix).astype(int):
-            q = O.f32_to_bf16(rng.standard_normal((1, 1, self.H_ix, self.D_ix)).astype(np.float32))
-            w = O.f32_to_bf16(rng.uniform(0, 0.01, (1, 1, self.H_ix)).astype(np.float32))
-            f = _freqs(1, self.rd, int(s)).numpy()
+        # chunks of consecutive rows spread over the sequence: a row's cost grows
+        # with its position, so the mean over evenly spread chunks is the mean row
+        for s0 in np.linspace(0, S - rows_per_chunk, n_ix).astype(int):
+            q = torch.randn(1, rows_per_chunk, self.H_ix, self.D_ix, generator=g).bfloat16()
+            w = (torch.rand(1, rows_per_chunk, self.H_ix, generator=g) *
+                 (self.D_ix ** -0.5 * self.H_ix ** -0.5)).bfloat16()
+            fc = _freqs_cis(rows_per_chunk, self.rd, int(s0))
             t0 = time.perf_counter()
-            O.indexer_forward(q, kx[:, : s + 1], w, f, self.rd, self.k, 1, 0, 0, s0=int(s))
+            R.indexer_after_projections(q, w, kx, fc, self.rd, self.k, 1, 0, 0, s0=int(s0))
             t_ix += time.perf_counter() - t0
-        kv = O.f32_to_bf16(rng.standard_normal((1, S, self.D_sa)).astype(np.float32))
-        q = O.f32_to_bf16(rng.standard_normal((1, n_sa, self.H_sa, self.D_sa)).astype(np.float32))
-        idx = np.stack([rng.permutation(S)[: self.k] for _ in range(n_sa)])[None].astype(np.int32)
+        kv = torch.randn(1, S, self.D_sa, generator=g).bfloat16()
+        q = torch.randn(1, n_sa, self.H_sa, self.D_sa, generator=g).bfloat16()
+        idx = torch.stack([torch.randperm(S, generator=g)[: self.k] for _ in range(n_sa)])[None].int()
         t0 = time.perf_counter()
-        O.sparse_attn(q, kv, np.zeros(self.H_sa, np.float32), idx, self.D_sa ** -0.5, self.dv)
+        R.sparse_attn(q, kv, torch.zeros(self.H_sa), idx, self.D_sa ** -0.5)
         t_sa = time.perf_counter() - t0
-        x = rng.standard_normal((n_sk, 8, 8)).astype(np.float32)
+        x = torch.randn(n_sk, 8, 8, generator=g)
         t0 = time.perf_counter()
-        O.sinkhorn(x, self.sk_repeat, 1e-6)
+        R.sinkhorn(x, self.sk_repeat, 1e-6)
         t_sk = time.perf_counter() - t0
         rows = self.B * S
         n_mats = self.sk_shape[0] * self.sk_shape[1]
-        t_step = t_ix / n_ix * rows + t_sa / n_sa * rows + t_sk / n_sk * n_mats
-        return rows / t_step, (f"{n_ix} indexer rows spread over positions 0..{S-1}, {n_sa} "
-                               f"sparse-attention rows, {n_sk} Sinkhorn matrices; time per row "
-                               f"extrapolated to the full step")
+        t_step = (t_ix / (n_ix * rows_per_chunk) * rows + t_sa / n_sa * rows +
+                  t_sk / n_sk * n_mats)
+        return rows / t_step, (f"the reference's torch forwards (oracle/ks_ref_torch.py) on "
+                               f"{torch.get_num_threads()} threads: {n_ix} chunks of "
+                               f"{rows_per_chunk} indexer rows spread over positions 0..{S-1}, "
+                               f"{n_sa} sparse-attention rows, {n_sk} Sinkhorn matrices; time "
+                               f"per row extrapolated to the full step")
 
 
 class SingleOp(Workload):
@@ -368,14 +385,17 @@ class SinkhornOp(SingleOp):
             self.op()
 
     def cpu_sample(self, budget_rows=None):
-        from oracle import ks_oracle as O
+        import torch
+        from oracle import ks_ref_torch as R
 
+        torch.set_num_threads(os.cpu_count() or 1)
         n = min(self.units, 65536)
-        x = np.random.default_rng(0).standard_normal((n, self.n, self.n)).astype(np.float32)
+        x = torch.randn(n, self.n, self.n, generator=torch.Generator().manual_seed(0))
         t0 = time.perf_counter()
-        O.sinkhorn(x, 20, 1e-6)
+        R.sinkhorn(x, 20, 1e-6)
         dt = time.perf_counter() - t0
-        return n / dt, f"{n} matrices"
+        return n / dt, (f"the reference's torch forward (oracle/ks_ref_torch.py) on "
+                        f"{torch.get_num_threads()} threads, {n} matrices")
 
 
 class SparseAttnOp(SingleOp):
@@ -443,17 +463,20 @@ class SparseAttnOp(SingleOp):
             self.op()
 
     def cpu_sample(self, budget_rows=(8,)):
-        from oracle import ks_oracle as O
+        import torch
+        from oracle import ks_ref_torch as R
 
-        rng = np.random.default_rng(0)
-        n = budget_rows[0]
-        kv = O.f32_to_bf16(rng.standard_normal((1, self.N, self.D)).astype(np.float32))
-        q = O.f32_to_bf16(rng.standard_normal((1, n, self.H, self.D)).astype(np.float32))
-        idx = np.stack([rng.permutation(self.N)[: self.K] for _ in range(n)])[None].astype(np.int32)
+        torch.set_num_threads(os.cpu_count() or 1)
+        g = torch.Generator().manual_seed(0)
+        n = max(budget_rows[0], 128 if self.cfg == "c2" else 8)
+        kv = torch.randn(1, self.N, self.D, generator=g).bfloat16()
+        q = torch.randn(1, n, self.H, self.D, generator=g).bfloat16()
+        idx = torch.stack([torch.randperm(self.N, generator=g)[: self.K] for _ in range(n)])[None].int()
         t0 = time.perf_counter()
-        O.sparse_attn(q, kv, np.zeros(self.H, np.float32), idx, self.D ** -0.5, self.dv)
+        R.sparse_attn(q, kv, torch.zeros(self.H), idx, self.D ** -0.5)
         dt = time.perf_counter() - t0
-        return n / dt, f"{n} query rows, time per row"
+        return n / dt, (f"the reference's torch forward (oracle/ks_ref_torch.py) on "
+                        f"{torch.get_num_threads()} threads, {n} query rows, time per row")
 
 
 class IndexerOp(SingleOp):
@@ -506,20 +529,26 @@ class IndexerOp(SingleOp):
                                  1, True, 0, pos0=a, out=self.out[i], workspace=self.ws)
 
     def cpu_sample(self, budget_rows=(8,)):
-        from oracle import ks_oracle as O
+        import torch
+        from oracle import ks_ref_torch as R
 
-        rng = np.random.default_rng(0)
-        n = budget_rows[0]
-        kx = O.f32_to_bf16(rng.standard_normal((1, self.T, self.D)).astype(np.float32))
+        torch.set_num_threads(os.cpu_count() or 1)
+        g = torch.Generator().manual_seed(0)
+        n, rows_per_chunk = budget_rows[0], min(32, self.S)
+        kx = torch.randn(1, self.T, self.D, generator=g).bfloat16()
         t_ix = 0.0
-        for s in np.linspace(self.row0, self.T - 1, n).astype(int):
-            q = O.f32_to_bf16(rng.standard_normal((1, 1, self.H, self.D)).astype(np.float32))
-            w = O.f32_to_bf16(rng.uniform(0, 0.01, (1, 1, self.H)).astype(np.float32))
+        for s0 in np.linspace(self.row0, self.T - rows_per_chunk, n).astype(int):
+            q = torch.randn(1, rows_per_chunk, self.H, self.D, generator=g).bfloat16()
+            w = (torch.rand(1, rows_per_chunk, self.H, generator=g) *
+                 (self.D ** -0.5 * self.H ** -0.5)).bfloat16()
             t0 = time.perf_counter()
-            O.indexer_forward(q, kx[:, : s + 1], w, _freqs(1, self.rd, int(s)).numpy(), self.rd,
-                              self.k, 1, 0, 0, s0=int(s))
+            R.indexer_after_projections(q, w, kx, _freqs_cis(rows_per_chunk, self.rd, int(s0)),
+                                        self.rd, self.k, 1, 0, 0, s0=int(s0))
             t_ix += time.perf_counter() - t0
-        return n / t_ix, f"{n} rows spread over positions {self.row0}..{self.T - 1}, time per row"
+        return n * rows_per_chunk / t_ix, (
+            f"the reference's torch forward (oracle/ks_ref_torch.py) on {torch.get_num_threads()} "
+            f"threads, {n} chunks of {rows_per_chunk} rows spread over positions "
+            f"{self.row0}..{self.T - 1}, time per row")
 
 
 class CopyPipeline:
@@ -943,8 +972,9 @@ def main():
 
 
 def reference_arm(a, rank, world):
-    """The reference algorithm (oracle port) on the host cores, each step a bounded
-    row sample of the workload, throughput extrapolated per row."""
+    """The reference algorithm (its torch forwards restated in oracle/, on the host
+    cores) on a bounded row sample of the workload per step, throughput
+    extrapolated per row."""
     if rank != 0:
         return
     wl = WORKLOADS[a.workload](0, world, None)

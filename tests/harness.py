@@ -15,9 +15,9 @@ forwards of baseline/*.py in torch, so the same comparison runs on the B200:
 * ``compare``          <- auto_bench.py:270-312 (compare_values, for tensors)
 * ``v0_class``         the reference Model of each op: constructor, parameter
   names and random draws come from the drop-in ``ModelNew`` (which keeps them
-  identical to the reference's), forward restated from
-  baseline/sinkhorn.py:13-19, baseline/sparse_attention.py:5-42 and
-  baseline/indexer.py:114-129,161-206 with the same torch operations.
+  identical to the reference's), forward from oracle/ks_ref_torch.py (the
+  reference's baseline/sinkhorn.py:13-19, baseline/sparse_attention.py:5-42 and
+  baseline/indexer.py:114-129,161-206 restated with the same torch operations).
 
 ``tests/test_harness_cpu.py`` pins the v0 restatements on the CPU against
 fixtures that the reference's own modules produced (tests/golden/hx_*.npz).
@@ -30,6 +30,8 @@ import sys
 import types
 
 import torch
+
+from oracle import ks_ref_torch as R
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(ROOT, "kernelswift_b200")
@@ -104,65 +106,25 @@ def to_device(v, device):
 
 
 # ---------------------------------------------------------------- v0 forwards
+# (the arithmetic lives in oracle/ks_ref_torch.py; these bind it to the modules)
 def _sinkhorn_v0(self, x):
-    """baseline/sinkhorn.py:13-19."""
-    y = x.softmax(-1) + self.eps
-    y = y / (y.sum(-2, keepdim=True) + self.eps)
-    for _ in range(self.repeat - 1):
-        y = y / (y.sum(-1, keepdim=True) + self.eps)
-        y = y / (y.sum(-2, keepdim=True) + self.eps)
-    return y
+    return R.sinkhorn(x, self.repeat, self.eps)
 
 
 def _sparse_attention_v0(self, q, kv, topk_idxs):
-    """baseline/sparse_attention.py:5-42: gather the selected kv rows (invalid ones
-    zeroed), fp32 scores, -inf on invalid entries, softmax with the sink in the
-    denominator, fp32 weighted sum, cast back to q's dtype."""
-    B, M, H, D = q.shape
-    K = topk_idxs.shape[-1]
-    ok = topk_idxs >= 0
-    rows = topk_idxs.clamp_min(0).long()
-    bidx = torch.arange(B, device=q.device)[:, None, None].expand(B, M, K)
-    g = kv[bidx, rows].masked_fill(~ok.unsqueeze(-1), 0.0)
-    s = torch.einsum("bmhd,bmtd->bmht", q.float(), g.float()) * self.softmax_scale
-    s = s.masked_fill(~ok.unsqueeze(2), float("-inf"))
-    sink = self.attn_sink.float().view(1, 1, H, 1)
-    z = torch.maximum(torch.amax(s, dim=-1, keepdim=True), sink)
-    e = torch.exp(s - z).masked_fill(~ok.unsqueeze(2), 0.0)
-    w = e / (e.sum(dim=-1, keepdim=True) + torch.exp(sink - z))
-    return torch.einsum("bmht,bmtd->bmhd", w, g.float()).to(q.dtype)
-
-
-def _rope_inplace(x, freqs_cis):
-    """baseline/indexer.py:114-129: rotate interleaved pairs of x (a view) by the
-    complex factors of its rows, computed in fp32 and copied back into x."""
-    cx = torch.view_as_complex(x.float().unflatten(-1, (-1, 2)))
-    f = freqs_cis.view(1, cx.size(1), 1, cx.size(-1))
-    x.copy_(torch.view_as_real(cx * f).flatten(-2))
+    return R.sparse_attn(q, kv, self.attn_sink, topk_idxs, self.softmax_scale)
 
 
 def _indexer_v0(self, x, qr, start_pos, offset):
     """baseline/indexer.py:161-206.  Also keeps the masked bf16 scores in
     ``self.last_scores`` for classifying index differences."""
-    B, S, _ = x.size()
-    end_pos = start_pos + S
-    ratio = self.compress_ratio
-    rd = self.rope_head_dim
+    S = x.size(1)
     q = self.wq_b(qr).unflatten(-1, (self.n_local_heads, self.head_dim))
-    _rope_inplace(q[..., -rd:], self.freqs_cis[start_pos:end_pos])
     w = self.weights_proj(x) * (self.softmax_scale * self.n_heads ** -0.5)
-    sc = torch.einsum("bshd,btd->bsht", q, self.kv_cache[:B, : end_pos // ratio])
-    sc = (sc.relu_() * w.unsqueeze(-1)).sum(dim=2)
-    if start_pos == 0:
-        keys = torch.arange(S // ratio, device=x.device).repeat(S, 1)
-        lim = torch.arange(1, S + 1, device=x.device).unsqueeze(1) // ratio
-        sc += torch.where(keys >= lim, float("-inf"), 0.0)
-    self.last_scores = sc
-    idx = sc.topk(min(self.index_topk, end_pos // ratio), dim=-1)[1]
-    if start_pos == 0:
-        lim = torch.arange(1, S + 1, device=x.device).unsqueeze(1) // ratio
-        return torch.where(idx >= lim, -1, idx + offset)
-    return idx + offset
+    idx, self.last_scores = R.indexer_after_projections(
+        q, w, self.kv_cache, self.freqs_cis[start_pos:start_pos + S], self.rope_head_dim,
+        self.index_topk, self.compress_ratio, start_pos, offset)
+    return idx
 
 
 _V0_FORWARD = {"sinkhorn": _sinkhorn_v0, "sparse_attention": _sparse_attention_v0,
