@@ -635,17 +635,22 @@ int ks_proj_rope(const void* a, const void* w, void* out, int64_t M, int64_t N, 
   p.rd = rope_dim;
   p.scale = scale;
   p.apply_scale = apply_scale ? 1 : 0;
+  if (rope_dim > 64) return fail(KS_ERR_UNSUPPORTED, "proj_rope: rope_dim=%d > 64", rope_dim);
   const size_t st_bytes = (size_t)PG_TILE_M * 128 + (size_t)n_tile * 128;
-  int stages = (int)((232448 - 2048) / st_bytes);
+  // per-row RoPE factors of the tile (epilogue), rows of rd + 2 words
+  const size_t fr_bytes = rope_dim > 0 ? round_up((int64_t)PG_TILE_M * (rope_dim + 2) * 4, 1024) : 0;
+  int stages = (int)((232448 - 2048 - fr_bytes) / st_bytes);
   if (stages > PG_MAX_STAGES) stages = PG_MAX_STAGES;
+  if (stages < 2) return fail(KS_ERR_UNSUPPORTED, "proj_rope: shared memory too small");
   p.stages = stages;
+  p.fr_off = (uint32_t)(1024 + (size_t)stages * st_bytes);
   p.tiles_m = (int)((M + PG_TILE_M - 1) / PG_TILE_M);
   p.tiles_n = (int)(N / n_tile);
   p.status = dev->status;
   p.budget_ns = wait_budget_ns();
   // at least half of the shared memory, so two CTAs never share an SM (each
   // allocates all 512 TMEM columns)
-  size_t smem = 1024 + 1024 + (size_t)stages * st_bytes;
+  size_t smem = 1024 + 1024 + (size_t)stages * st_bytes + fr_bytes;
   if (smem < 120 * 1024) smem = 120 * 1024;
   CUtensorMap am, bm;
   if (int rc = make_map_bf16(&am, a, K, (uint64_t)M, K * 2, 64, PG_TILE_M)) return rc;

@@ -37,6 +37,7 @@ struct ProjParams {
   int32_t apply_scale;
   int32_t stages;
   int32_t tiles_m, tiles_n;
+  uint32_t fr_off;      // shared-memory offset of the per-row RoPE factors (rd > 0)
   int* status;
   uint64_t budget_ns;
 };
@@ -144,6 +145,11 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     const int quarter = warp & 3;  // TMEM lanes [32 quarter, +32)
     const int row_in_tile = quarter * 32 + lane;
     const int rope0 = p.hd - p.rd;  // first rotated column of a head
+    // this thread's row of RoPE factors (cos, sin pairs), staged once per tile: a
+    // load per rotated pair from global memory would put one memory latency on
+    // every 16 columns.  Row stride rd + 2 words: a warp's 8-byte reads of one pair
+    // index fall on distinct banks within each half-warp.
+    float* my_fr = reinterpret_cast<float*>(smem + p.fr_off) + row_in_tile * (p.rd + 2);
     uint32_t ac = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++ac) {
       const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
@@ -152,7 +158,16 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
       tc_fence_after();
       const int m = tm * PG_TILE_M + row_in_tile;
       const bool row_ok = m < p.M;
-      const float* fr = p.freqs + (int64_t)(row_ok ? m % p.S : 0) * p.rd;
+      if (p.rd > 0) {
+        const float2* fr = reinterpret_cast<const float2*>(p.freqs + (int64_t)(row_ok ? m % p.S : 0) * p.rd);
+        float2 f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < p.rd / 2) f[j] = __ldg(fr + j);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < p.rd / 2) reinterpret_cast<float2*>(my_fr)[j] = f[j];
+      }
       uint16_t* orow = p.out + (int64_t)m * p.N + (int64_t)tn * p.n_tile;
       const uint32_t tbase = tmem + as * 256 + ((uint32_t)(quarter * 32) << 16);
       for (int c = 0; c < p.n_tile; c += 16) {
@@ -168,7 +183,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
           const int d = d0 + 2 * i;
           if (p.rd > 0 && d >= rope0 && row_ok) {
             const int j = (d - rope0) >> 1;
-            const float2 cs = __ldg(reinterpret_cast<const float2*>(fr) + j);
+            const float2 cs = reinterpret_cast<const float2*>(my_fr)[j];
             const float xr = bf16lo_f32(v), xi = bf16hi_f32(v);
             const float re = __fsub_rn(__fmul_rn(xr, cs.x), __fmul_rn(xi, cs.y));
             const float im = __fadd_rn(__fmul_rn(xr, cs.y), __fmul_rn(xi, cs.x));
