@@ -308,7 +308,9 @@ int topk_impl(const void* scores, int64_t score_ld, int64_t B, int64_t S, int64_
   // composites sorted per row: TK_THREADS * ept >= kpow2
   const int ept = kpow2 <= TK_THREADS ? 1 : kpow2 / TK_THREADS;
   const size_t nbuf = (size_t)TK_THREADS * ept > (size_t)TK_HBINS ? (size_t)TK_THREADS * ept : (size_t)TK_HBINS;
-  const size_t smem = nbuf * 4 + (TK_WARPS + 4 + 8 + 2 * TK_WARPS) * 4 + round_up(T, 8) * 2;
+  // the staged keys, reused by the counting sort's per-warp counters
+  const size_t key_bytes = std::max<size_t>((size_t)round_up(T, 8) * 2, (size_t)TK_WARPS * TK_CBINS * 2);
+  const size_t smem = nbuf * 4 + (TK_WARPS + 4 + 8 + 2 * TK_WARPS) * 4 + key_bytes;
   switch (ept) {
     case 1: return launch_topk<1>(dev, p, B * S, smem, st);
     case 2: return launch_topk<2>(dev, p, B * S, smem, st);

@@ -24,14 +24,16 @@
 //   2. one pass in index order compacts the selected (key, index) pairs with one
 //      block-wide exclusive scan per 4096-element chunk (counts of keys above and
 //      equal to `thr` packed into one word);
-//   3. a stable counting sort when the selected keys span at most 128 values (see
-//      below), else a bitonic sort of the 32-bit composites ((0xFFFF-key)<<16 | index) puts
+//   3. a stable counting sort when the selected keys span fewer than TK_CBINS values
+//      (see below), else a bitonic sort of the 32-bit composites ((0xFFFF-key)<<16 | index) puts
 //      them in (value desc, index asc) order; the composites are all distinct.
 //      Each thread holds EPT consecutive composites in registers: strides below
 //      EPT are exchanged in registers, strides within a warp by shuffles, and only
 //      the strides across warps go through shared memory;
 //   4. the post-processed indices are written as int64 or int32.
 #pragma once
+#include <type_traits>
+
 #include "ks_device.cuh"
 
 namespace ks {
@@ -43,7 +45,7 @@ constexpr int TK_CHUNK = TK_THREADS * TK_PER_THREAD;
 constexpr int TK_HBITS = 10;                 // first-pass histogram: at most 1024 bins
 constexpr int TK_HBINS = 1 << TK_HBITS;
 constexpr int TK_HPER = TK_HBINS / TK_THREADS;
-constexpr int TK_CBINS = 128;                // counting sort: at most 128 distinct keys
+constexpr int TK_CBINS = 1024;               // counting sort: selection spans < 1024 key values
 
 struct TopkParams {
   const uint16_t* scores;  // bf16 bits, row r at scores + r * row_stride
@@ -123,7 +125,7 @@ __device__ __forceinline__ void find_bin_desc(const uint32_t* hist, int nbins, u
 }
 
 template <int EPT>
-__global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
+__global__ void __launch_bounds__(TK_THREADS, 3) topk_rows_kernel(TopkParams p) {
   constexpr int NS = TK_THREADS * EPT;  // sorted composites, >= kpow2
   constexpr int NBUF = NS > TK_HBINS ? NS : TK_HBINS;
   extern __shared__ __align__(16) uint8_t tk_smem[];
@@ -332,15 +334,19 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
   // counters live in the staged-key area, which the compaction has finished with.
   {
     const uint32_t lo = need_select ? thr : kmin;
-    const bool use_count = nsel > 0 && kmax - lo < (uint32_t)TK_CBINS &&
-                           (size_t)((p.T + 7) & ~7) * 2 >= (size_t)TK_WARPS * TK_CBINS * 2;
-    if (use_count) {  // block-uniform
-      uint16_t* cnt = keys;  // [TK_WARPS][TK_CBINS]
-      for (int i = tid; i < TK_WARPS * TK_CBINS; i += TK_THREADS) cnt[i] = 0;
+    // CB key values (bins): 128 covers the selections of long score rows (a few
+    // dozen values); up to TK_CBINS covers rows shorter than k, whose selection
+    // is the whole row (a few hundred values).  The per-warp counters live in the
+    // staged-key area, which the host sizes for TK_WARPS x TK_CBINS of them.
+    auto count_sort = [&](auto cb_tag) {
+      constexpr int CB = decltype(cb_tag)::value;
+      constexpr int BPT = CB > TK_THREADS ? CB / TK_THREADS : 1;  // key values per thread
+      uint16_t* cnt = keys;  // [TK_WARPS][CB]
+      for (int i = tid; i < TK_WARPS * CB; i += TK_THREADS) cnt[i] = 0;
       __syncthreads();
       const int seg = (nsel + TK_THREADS - 1) / TK_THREADS * 32;
       const int s0 = warp * seg, s1 = min(nsel, s0 + seg);
-      uint16_t* wc = cnt + warp * TK_CBINS;
+      uint16_t* wc = cnt + warp * CB;
       for (int b = s0; b < s1; b += 32) {
         const int i = b + lane;
         const uint32_t d = i < s1 ? kmax - (0xFFFFu - (sortbuf[i] >> 16)) : 0xFFFFFFFFu;
@@ -349,19 +355,31 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
         __syncwarp();
       }
       __syncthreads();
-      // exclusive prefix over warps per key, then over keys (descending key = ascending d)
-      uint32_t tot_b = 0;
-      if (tid < TK_CBINS) {
-        for (int w = 0; w < TK_WARPS; ++w) {
-          const uint32_t c = cnt[w * TK_CBINS + tid];
-          cnt[w * TK_CBINS + tid] = (uint16_t)tot_b;
-          tot_b += c;
+      // exclusive prefix over warps per key, then over keys (descending key =
+      // ascending d); thread t owns the key values t BPT .. t BPT + BPT - 1
+      uint32_t tot_b[BPT], tsum = 0;
+#pragma unroll
+      for (int j = 0; j < BPT; ++j) {
+        const int d = tid * BPT + j;
+        tot_b[j] = 0;
+        if (d < CB) {
+          for (int w = 0; w < TK_WARPS; ++w) {
+            const uint32_t c = cnt[w * CB + d];
+            cnt[w * CB + d] = (uint16_t)tot_b[j];
+            tot_b[j] += c;
+          }
         }
+        tsum += tot_b[j];
       }
       uint32_t total;
-      const uint32_t kbase = block_excl_scan(tid < TK_CBINS ? tot_b : 0u, warp_tot, total);
-      if (tid < TK_CBINS)
-        for (int w = 0; w < TK_WARPS; ++w) cnt[w * TK_CBINS + tid] += (uint16_t)kbase;
+      uint32_t kbase = block_excl_scan(tsum, warp_tot, total);
+#pragma unroll
+      for (int j = 0; j < BPT; ++j) {
+        const int d = tid * BPT + j;
+        if (d < CB)
+          for (int w = 0; w < TK_WARPS; ++w) cnt[w * CB + d] += (uint16_t)kbase;
+        kbase += tot_b[j];
+      }
       __syncthreads();
       const uint32_t lt = (1u << lane) - 1u;
       for (int b = s0; b < s1; b += 32) {
@@ -375,6 +393,13 @@ __global__ void __launch_bounds__(TK_THREADS) topk_rows_kernel(TopkParams p) {
         __syncwarp();
       }
       for (int i = nsel + tid; i < K; i += TK_THREADS) write_out(i, false, 0u);
+    };
+    if (nsel > 0 && kmax - lo < 128u) {  // block-uniform
+      count_sort(std::integral_constant<int, 128>{});
+      return;
+    }
+    if (nsel > 0 && kmax - lo < (uint32_t)TK_CBINS) {
+      count_sort(std::integral_constant<int, TK_CBINS>{});
       return;
     }
   }
