@@ -224,9 +224,11 @@ class DsaE2E(Workload):
                        lambda: ops.sinkhorn(self.sk_x, self.sk_repeat, 1e-6, out=self.sk_out)))
         return pieces
 
+    e2e_rows = 4096  # query rows per piece of the host-buffer pipeline
+
     def _pipeline(self):
         if getattr(self, "_pipe", None) is None:
-            self._pipe = CopyPipeline(self.e2e_pieces())
+            self._pipe = CopyPipeline(self.e2e_pieces(self.e2e_rows))
         return self._pipe
 
     def run_e2e(self):
@@ -239,7 +241,7 @@ class DsaE2E(Workload):
         self._pipeline().end()
 
     def e2e_note(self):
-        return (f"{len(self._pipeline().pieces)} pieces per step (<= 4096 query rows each): "
+        return (f"{len(self._pipeline().pieces)} pieces per step (<= {self.e2e_rows} query rows each): "
                 "host->device copies, the ops (ops.dsa: indexer -> sparse attention in one library "
                 "call; ops.sinkhorn) and device->host copies on three streams, piece by piece, so "
                 "copies in both directions overlap the kernels and each other")
@@ -724,6 +726,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-rows", type=int, default=None,
+                    help="query rows per piece of the host-buffer (e2e) pipeline")
     ap.add_argument("--no-per-op", action="store_true",
                     help="skip the per-operator block of the default workload's line")
     ap.add_argument("--tokens", type=int, default=None,
@@ -904,6 +908,8 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
     wl = WORKLOADS[a.workload](rank, world, device, tokens=a.tokens) if a.tokens else WORKLOADS[a.workload](rank, world, device)
+    if a.e2e_rows:
+        wl.e2e_rows = a.e2e_rows
     from kernelswift_b200 import ops
 
     for _ in range(a.warmup):
