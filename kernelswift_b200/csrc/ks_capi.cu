@@ -641,28 +641,37 @@ int ks_proj_rope(const void* a, const void* w, void* out, int64_t M, int64_t N, 
   const size_t st_bytes = (size_t)PG_TILE_M * 128 + (size_t)n_tile * 128;
   // per-row RoPE factors of the tile (epilogue), rows of rd + 2 words
   const size_t fr_bytes = rope_dim > 0 ? round_up((int64_t)PG_TILE_M * (rope_dim + 2) * 4, 1024) : 0;
-  int stages = (int)((232448 - 2048 - fr_bytes) / st_bytes);
+  // output through TMA stores (boxes of 64 columns) when a tile is at least that wide
+  p.tma_store = n_tile >= 64 ? 1 : 0;
+  const size_t out_stage = p.tma_store ? 32768 : 0;
+  int stages = (int)((232448 - 2048 - fr_bytes - out_stage) / st_bytes);
   if (stages > PG_MAX_STAGES) stages = PG_MAX_STAGES;
   if (stages < 2) return fail(KS_ERR_UNSUPPORTED, "proj_rope: shared memory too small");
   p.stages = stages;
   p.fr_off = (uint32_t)(1024 + (size_t)stages * st_bytes);
+  p.st_off = (uint32_t)(p.fr_off + fr_bytes);
   p.tiles_m = (int)((M + PG_TILE_M - 1) / PG_TILE_M);
   p.tiles_n = (int)(N / n_tile);
   p.status = dev->status;
   p.budget_ns = wait_budget_ns();
   // at least half of the shared memory, so two CTAs never share an SM (each
   // allocates all 512 TMEM columns)
-  size_t smem = 1024 + 1024 + (size_t)stages * st_bytes + fr_bytes;
+  size_t smem = 1024 + 1024 + (size_t)stages * st_bytes + fr_bytes + out_stage;
   if (smem < 120 * 1024) smem = 120 * 1024;
-  CUtensorMap am, bm;
+  CUtensorMap am, bm, om;
   if (int rc = make_map_bf16(&am, a, K, (uint64_t)M, K * 2, 64, PG_TILE_M)) return rc;
   if (int rc = make_map_bf16(&bm, w, K, (uint64_t)N, K * 2, 64, n_tile)) return rc;
+  if (p.tma_store) {
+    if (int rc = make_map_bf16(&om, out, N, (uint64_t)M, N * 2, 64, 32)) return rc;
+  } else {
+    om = am;  // unused
+  }
   if (int rc = smem_optin(dev, reinterpret_cast<const void*>(proj_gemm_kernel),
                           "cudaFuncSetAttribute(proj_gemm)"))
     return rc;
   const int64_t tiles = (int64_t)p.tiles_m * p.tiles_n;
   const int grid = (int)(tiles < dev->num_sms ? tiles : dev->num_sms);
-  proj_gemm_kernel<<<grid, PG_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(am, bm, p);
+  proj_gemm_kernel<<<grid, PG_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(am, bm, om, p);
   return launch_check("proj_gemm_kernel launch");
 }
 

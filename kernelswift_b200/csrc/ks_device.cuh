@@ -229,6 +229,29 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* m, uint64_t* bar,
       : "memory");
 }
 
+// 2D tile store from this CTA's shared memory to global memory, tracked as a bulk
+// group of the issuing thread (x, y >= 0; x times the element size a multiple of 16).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int32_t x,
+                                             int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until at most N of this thread's bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until at most N of this thread's bulk groups are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Four rows (y0..y3) of a 2D tensor, columns [x, x + box_w), into four consecutive
 // box rows in this CTA's shared memory.  No multicast.
 __device__ __forceinline__ void tma_gather4(const CUtensorMap* m, uint64_t* bar, void* dst,
