@@ -271,8 +271,8 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Thread = key (TMEM lane); two tokens at a time, their head sums carried
-    // as one f32x2 pair (each token still summed in head order, round to nearest).
+    // Thread = key (TMEM lane); two tokens at a time, each summed in head order
+    // with round-to-nearest fp32 adds (F8: the pair carried as one f32x2 value).
     const int e = warp - IX_EPI_WARP0;  // 0..7
     const int quarter = warp & 3;       // TMEM lanes [32*quarter, +32) belong to this warp
     const int half = e >> 2;            // which half of the item's tokens
@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
           const uint16_t* wrow0 = sh->wbuf + j0 * H;
           const uint16_t* wrow1 = wrow0 + H;
           const uint32_t col0 = tmem + as * IX_N + j0 * H + ((uint32_t)(quarter * 32) << 16);
-          uint64_t acc = 0;  // (token s0, token s1) partial sums, f32x2
+          float acc0 = 0.f, acc1 = 0.f;  // token s0, token s1 partial sums
 #pragma unroll
           for (int c = 0; c < H; c += 16) {
             uint32_t r0[16], r1[16];
@@ -416,15 +416,15 @@ __global__ void __launch_bounds__(IX_THREADS, 1)
             for (int h = 0; h < 16; h += 2) {
               const uint32_t p0 = mul_bf16x2(cvt_relu_bf16x2(__uint_as_float(r0[h]), __uint_as_float(r0[h + 1])), w0[h >> 1]);
               const uint32_t p1 = mul_bf16x2(cvt_relu_bf16x2(__uint_as_float(r1[h]), __uint_as_float(r1[h + 1])), w1[h >> 1]);
-              // head h (low halves), then head h + 1 (high halves)
-              asm("{ .reg .b64 t; mov.b64 t, {%1, %2}; add.rn.f32x2 %0, %0, t; }"
-                  : "+l"(acc) : "r"(p0 << 16), "r"(p1 << 16));
-              asm("{ .reg .b64 t; mov.b64 t, {%1, %2}; add.rn.f32x2 %0, %0, t; }"
-                  : "+l"(acc) : "r"(p0 & 0xFFFF0000u), "r"(p1 & 0xFFFF0000u));
+              // head h (low halves), then head h + 1 (high halves): a mixed-precision
+              // add takes the bf16 half as it is (exact widening, fp32 round-to-nearest
+              // sum), with no separate unpacking of the pair
+              asm("{ .reg .b16 l0, h0, l1, h1; mov.b32 {l0, h0}, %2; mov.b32 {l1, h1}, %3;"
+                  " add.rn.f32.bf16 %0, l0, %0; add.rn.f32.bf16 %1, l1, %1;"
+                  " add.rn.f32.bf16 %0, h0, %0; add.rn.f32.bf16 %1, h1, %1; }"
+                  : "+f"(acc0), "+f"(acc1) : "r"(p0), "r"(p1));
             }
           }
-          float acc0, acc1;
-          asm("mov.b64 {%0, %1}, %2;" : "=f"(acc0), "=f"(acc1) : "l"(acc));
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int s = u ? s1 : s0;
