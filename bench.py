@@ -946,7 +946,11 @@ def main():
         t = torch.tensor([e0.elapsed_time(e1) / a.steps], device=device)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        h2d, d2h = wl.e2e_bytes()
+        h2d, d2h = wl.e2e_bytes()  # this rank's copies; the line reports the whole job's
+        if world > 1:
+            nb = torch.tensor([h2d, d2h], dtype=torch.int64, device=device)
+            dist.all_reduce(nb, op=dist.ReduceOp.SUM)
+            h2d, d2h = int(nb[0].item()), int(nb[1].item())
         e2e = {"value": wl.units / (float(t.item()) / 1e3), "unit": wl.metric,
                "ms_per_step": float(t.item()), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "copies": wl.e2e_note()}
