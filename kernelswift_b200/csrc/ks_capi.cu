@@ -52,6 +52,10 @@ struct Device {
   // (cudaFuncSetAttribute acts on the current device's context only)
   const void* smem_optin[16] = {};
   int n_smem_optin = 0;
+  // co-resident CTA pairs of the persistent attention kernel, for the shared
+  // memory size it was last asked for
+  int sa_clusters = 0;
+  size_t sa_clusters_smem = 0;
 };
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
@@ -424,7 +428,25 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
   if (int rc = smem_optin(dev, reinterpret_cast<const void*>(sparse_attn_kernel),
                           "cudaFuncSetAttribute(sparse_attn)"))
     return rc;
-  sparse_attn_kernel<<<(unsigned)(2 * B * M), SA_THREADS, smem, st>>>(qm, p);
+  // Persistent: as many CTA pairs as can be resident at once (pairs must sit in
+  // one GPC, so this can be below num_sms / 2), at most one per token.
+  if (dev->sa_clusters_smem != smem) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (unsigned)dev->num_sms);
+    cfg.blockDim = dim3(SA_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(sparse_attn_kernel), &cfg);
+    if (e != cudaSuccess || n < 1) {
+      (void)cudaGetLastError();
+      n = dev->num_sms / 2;
+    }
+    dev->sa_clusters = n;
+    dev->sa_clusters_smem = smem;
+  }
+  const int64_t clusters = std::min<int64_t>(B * M, dev->sa_clusters);
+  sparse_attn_kernel<<<(unsigned)(2 * clusters), SA_THREADS, smem, st>>>(qm, p);
   return launch_check("sparse_attn_kernel launch");
 }
 

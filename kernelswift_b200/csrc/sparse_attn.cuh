@@ -1,4 +1,5 @@
-// Top-k sparse attention with a per-head sink on tcgen05, one CTA pair per query.
+// Top-k sparse attention with a per-head sink on tcgen05, one CTA pair per query
+// token at a time, persistent over the tokens.
 //
 // Semantics follow baseline/sparse_attention.py:5-42 of KernelSwift:
 //   s_t   = (q_h . kv[idx_t]) * scale, entries with idx_t < 0 masked out
@@ -38,11 +39,21 @@
 // 48 GB/s with 16 issuing warps.  Per 256 keys an SM runs 36 + 32 MMAs of 64
 // tensor cycles each and gathers ~272 KB.
 //
+// Persistent CTA pairs.  Each cluster takes tokens cid, cid + clusters, ... in
+// turn; the ring, every barrier phase and the S/P buffers continue from one
+// token to the next (global block index), so the next token's gathers, query
+// tile and first QK blocks overlap the previous token's last PV and epilogue.
+// The query tile is reloaded once the token's last QK MMAs have read it
+// ("q_free", committed by the QK issuer to both CTAs); a token's first PV (which
+// overwrites O) waits for its P, which the softmax warps write only after they
+// have read the previous token's O out.
+//
 // Roles per CTA (16 warps; registers are granted per four warps, so 13 would
 // cost the same):
 //   warps 0-7   four gather groups (warps 2g, 2g + 1),
-//   warps 8, 9  issue the MMAs in CTA 0: warp 8 the QK chunks, warp 9 the V
-//               chunks; in CTA 1 warp 8 forwards "query tile landed",
+//   warps 8, 9  issue the MMAs in CTA 0: warp 8 the QK chunks (and loads the
+//               leader's query tiles), warp 9 the V chunks; in CTA 1 warp 8
+//               loads that CTA's query tiles and forwards "query tile landed",
 //   warps 10-11 a fifth gather group,
 //   warps 12-15 online softmax (base 2, lazy rescaling of O when the running max
 //               grows by more than 2^8) and the epilogue.
@@ -102,7 +113,7 @@ struct SaShared {
   uint64_t acc_full[2], s_free[2];
   // per P buffer: with two buffers the softmax can finish P(j + 1) before the V
   // issuer has seen P(j), so one barrier would run two phases ahead of its waiter
-  uint64_t p_full[2], p_free[2], o_full, q_full, peer_q, drain_s, drain_v;
+  uint64_t p_full[2], p_free[2], o_full, q_full, q_free, peer_q, drain_s, drain_v;
   uint64_t xchg[3];
   uint32_t tmem_base;
   int abort;
@@ -139,8 +150,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
   uint8_t* ps = smem + p.p_off;
 
   const uint32_t cta = cluster_ctarank();
-  const int64_t token = blockIdx.x >> 1;
-  const int b = (int)(token / p.M);
+  // this cluster's tokens: cid, cid + ncl, ... (n_it of them; the grid has at
+  // most one cluster per token)
+  const int64_t n_tok = (int64_t)p.B * p.M;
+  const int64_t cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  const int n_it = (int)((n_tok - cid + ncl - 1) / ncl);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = p.D / 64;
   WaitCtx wc{&sh->abort, p.status, p.budget_ns};
@@ -161,6 +175,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
     mbar_init(&sh->p_free[1], 1);
     mbar_init(&sh->o_full, 1);
     mbar_init(&sh->q_full, 1);  // TMA of the query tile
+    mbar_init(&sh->q_free, 1);  // the token's last QK MMAs have read it (commit, both CTAs)
     mbar_init(&sh->peer_q, 1);
     mbar_init(&sh->drain_s, 1);
     mbar_init(&sh->drain_v, 1);
@@ -176,20 +191,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
-  const int32_t* ip = p.idx + token * p.K;
-  const uint16_t* kvb = p.kv + (int64_t)b * p.N * p.D;
   // Indices are fetched raw (-1 past K) well before they are used and checked
   // only then, so no thread waits on an index load; a masked key (negative or
   // beyond N) is gathered as zeros.  Likewise the row loads are predicated loads
   // that nothing reads until the shared-memory store.
-  auto idx_raw = [&](int key) -> int32_t { return ldg_s32_or(ip + key, key < p.K, -1); };
   auto idx_ok = [&](int32_t v) -> bool { return v >= 0 && v < p.N; };
+  // query tile of token `tok` (this CTA's 64 heads) into qs, completing on q_full
+  auto load_q = [&](int64_t tok) {
+    mbar_expect_tx(&sh->q_full, (uint32_t)nkb * 8192u);
+    const int32_t qrow = (int32_t)(tok * p.H + cta * 64);
+    for (int d = 0; d < nkb; ++d) tma_load_2d(&qmap, &sh->q_full, qs + d * 8192, d * 64, qrow);
+  };
 
   // Ring position n -> chunk: S(0) first, then per period p = 1..nblk the
   // chunks S(p) (p < nblk) followed by V(p - 1).  is_v: V chunk; blk: its block;
   // sub: dims chunk (QK) or 32-key chunk (V).
   const uint32_t period = (uint32_t)(nkb + SA_NKC);
-  const uint32_t n_total = (uint32_t)p.nblk * period;
+  const uint32_t n_total = (uint32_t)p.nblk * period;  // ring positions per token
+  const uint32_t n_all = (uint32_t)n_it * n_total;       // ... of all this cluster's tokens
   auto decode = [&](uint32_t n, bool& is_v, int& blk, int& sub) {
     if (n < (uint32_t)nkb) {
       is_v = false; blk = 0; sub = (int)n;
@@ -218,12 +237,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
     const int u = ((warp & 1) << 5) | lane;
     const int c = u & 7, rg = u >> 3;
     const uint32_t swz = (uint32_t)((c ^ rg) << 4);
-    if (threadIdx.x == 0) {
-      tma_prefetch_desc(&qmap);
-      mbar_expect_tx(&sh->q_full, (uint32_t)nkb * 8192u);
-      const int32_t qrow = (int32_t)(token * p.H + cta * 64);
-      for (int d = 0; d < nkb; ++d) tma_load_2d(&qmap, &sh->q_full, qs + d * 8192, d * 64, qrow);
-    }
     int colv[4];
     bool colin[4];
 #pragma unroll
@@ -231,26 +244,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       colv[s] = s < p.n_pvblk ? p.dv_begin + p.pv_col[cta][s] + 8 * c : 0;
       colin[s] = s < p.n_pvblk && colv[s] < p.D;
     }
+    // This group's chunks are ring positions ng = g, g + 5, ... of the cluster's
+    // token sequence; (it, n) = (token iteration, position in that token) is
+    // advanced alongside, without a division (n_total >= 9 > SA_GROUPS, so a
+    // step crosses at most one token boundary).
+    auto step = [&](uint32_t& n, int& it) {
+      n += SA_GROUPS;
+      if (n >= n_total) {
+        n -= n_total;
+        ++it;
+      }
+    };
     int32_t nidx[16];
-    auto fetch = [&](uint32_t n) {
-      if (n >= n_total) return;
+    int ip_it = -1;  // token iteration ip belongs to
+    const int32_t* ip = p.idx;
+    // raw indices of chunk (it, n), fetched one round ahead of its loads
+    auto fetch = [&](uint32_t n, int it) {
+      if (it != ip_it) {
+        ip_it = it;
+        ip = p.idx + (cid + (int64_t)it * ncl) * p.K;
+      }
       bool is_v;
       int blk, sub;
       decode(n, is_v, blk, sub);
       if (!is_v) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) nidx[i] = idx_raw(blk * SA_NB + (int)cta * SA_HALF + rg + 8 * i);
+        for (int i = 0; i < 16; ++i) {
+          const int key = blk * SA_NB + (int)cta * SA_HALF + rg + 8 * i;
+          nidx[i] = ldg_s32_or(ip + key, key < p.K, -1);
+        }
       } else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) nidx[i] = idx_raw(blk * SA_NB + sub * SA_KC + rg + 8 * i);
+        for (int i = 0; i < 4; ++i) {
+          const int key = blk * SA_NB + sub * SA_KC + rg + 8 * i;
+          nidx[i] = ldg_s32_or(ip + key, key < p.K, -1);
+        }
       }
     };
-    fetch((uint32_t)g);
+    uint32_t nc = (uint32_t)g, nf = (uint32_t)g;  // this chunk, the next fetch
+    int ic = 0, ifc = 0;
+    if ((uint32_t)g < n_all) fetch(nf, ifc);
+    step(nf, ifc);
+    int kv_it = -1;  // token iteration kvb belongs to
+    const uint16_t* kvb = p.kv;
     bool ok = true;
-    for (uint32_t n = (uint32_t)g; ok && n < n_total; n += SA_GROUPS) {
+    for (uint32_t ng = (uint32_t)g; ok && ng < n_all; ng += SA_GROUPS) {
+      if (ic != kv_it) {
+        kv_it = ic;
+        kvb = p.kv + (int64_t)((int)(cid + (int64_t)ic * ncl) / p.M) * p.N * p.D;  // token < 2^31
+      }
       bool is_v;
       int blk, sub;
-      decode(n, is_v, blk, sub);
+      decode(nc, is_v, blk, sub);
       uint4 v[16];
       if (!is_v) {
 #pragma unroll
@@ -265,14 +310,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
           for (int s = 0; s < 4; ++s) v[4 * i + s] = ldcg_or_zero(row + colv[s], colin[s] && rok);
         }
       }
-      fetch(n + SA_GROUPS);
+      step(nc, ic);
+      if (ng + SA_GROUPS < n_all) fetch(nf, ifc);
+      step(nf, ifc);
       // n_slots is a multiple of SA_GROUPS, so this group alone fills this slot
       // and its parity wait is never two phases ahead of the barrier.
-      const int slot = (int)(n % (uint32_t)p.n_slots);
-      wc.tag = (int)n;
-      if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->empty[slot], ((n / p.n_slots) & 1) ^ 1, wc))))
+      const int slot = (int)(ng % (uint32_t)p.n_slots);
+      wc.tag = (int)ng;
+      if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->empty[slot], ((ng / p.n_slots) & 1) ^ 1, wc))))
         break;
-      if (u == 0) KS_SA_TRACE(g, n / SA_GROUPS);
+      if (u == 0) KS_SA_TRACE(g, ng / SA_GROUPS);
       uint8_t* dst = smem + p.r_off + slot * SA_SLOT;
       if (!is_v) {
 #pragma unroll
@@ -287,21 +334,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
               *reinterpret_cast<uint4*>(dst + s * SA_VSEG + (rg + 8 * i) * 128 + swz) = v[4 * i + s];
       }
       sa_warp_ready(is_v ? &sh->full_v[slot] : &sh->full_s[slot], cta, lane);
-      if (u == 0) KS_SA_TRACE(4 + g, n / SA_GROUPS);
+      if (u == 0) KS_SA_TRACE(4 + g, ng / SA_GROUPS);
     }
     if (threadIdx.x == 0) {
-      mbar_wait(&sh->q_full, 0, wc, false, true);
       // Tail: the tensor cores signal "slot consumed" asynchronously, also into
       // this CTA from the leader's commits.  Wait until the last signal of every
       // slot has landed, so none can reach the barriers of the next CTA that
       // this SM runs.
       // (Skipped after an abort: the waits would only run out their budgets.)
       for (int sl = 0; sl < p.n_slots && !*wc.abort; ++sl) {
-        const uint32_t uses = (n_total + (uint32_t)(p.n_slots - 1 - sl)) / (uint32_t)p.n_slots;
+        const uint32_t uses = (n_all + (uint32_t)(p.n_slots - 1 - sl)) / (uint32_t)p.n_slots;
         if (uses > 0) mbar_wait(&sh->empty[sl], (uses - 1) & 1, wc, false, true);
       }
     }
   } else if (warp == SA_MMA_WARP || warp == SA_MMA_WARP + 1) {
+    int q_loads = 0;  // query tile loads issued (lane 0 of warp 8)
+    if (warp == SA_MMA_WARP && lane == 0) {
+      tma_prefetch_desc(&qmap);
+      load_q(cid);  // the first token's query tile (this CTA's heads)
+      q_loads = 1;
+    }
+    __syncwarp();
     if (cta == 0) {
       // ---------------------------------------------------------- MMA issuers (leader CTA)
       // Two warps: warp 8 issues the QK chunks, warp 9 the V chunks, each in
@@ -318,20 +371,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       // this warp.
       const bool v_issuer = warp != SA_MMA_WARP;
       const bool leader = elect_one();
-      bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->q_full, 0, wc) &&
-                                            mbar_wait(&sh->peer_q, 0, wc, true));
+      bool ok = true;
       // Descriptors are built once; a byte offset o moves the start address field by o / 16.
       const uint64_t rd0 = sdesc_sw128(smem_u32(smem + p.r_off), v_issuer ? SA_VSEG : 16, 1024);
       uint32_t ph = 0;  // bit k: parity of the next phase of slot k's full barrier for this stream
       // Ring position (rn) and slot (rs = rn mod n_slots) of this stream's next
       // chunk, advanced incrementally: the per-chunk work is a short dependent
-      // chain, so it carries no division.  Ring order S(0) | S(1) V(0) |
-      // S(2) V(1) | ... | V(nblk-1): the QK stream starts at 0 and skips V(j-2)
-      // before S(j), j >= 2; the V stream starts after S(1) and skips S(j+2) after V(j).
+      // chain, so it carries no division.  Per token the ring order is S(0) |
+      // S(1) V(0) | S(2) V(1) | ... | V(nblk-1): the QK stream starts at the
+      // token's first position and skips V(j-2) before S(j), j >= 2, and the last
+      // two V blocks after S(nblk-1); the V stream starts after S(1) and skips
+      // S(j+2) after V(j), and the next token's S(0) S(1) after V(nblk-1).
       const int ns = p.n_slots;
-      uint32_t rn = v_issuer ? (uint32_t)(nkb + (p.nblk > 1 ? nkb : 0)) : 0u;
+      const int s01 = nkb + (p.nblk > 1 ? nkb : 0);  // S(0) S(1)
+      uint32_t rn = v_issuer ? (uint32_t)s01 : 0u;
       int rs = (int)(rn % (uint32_t)ns);
-      auto adv = [&](int k) {
+      auto adv = [&](int k) {  // k <= 2 nkb: a few subtractions, no division
         rn += (uint32_t)k;
         rs += k;
         while (rs >= ns) rs -= ns;
@@ -355,31 +410,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         const uint32_t qlo = (uint32_t)qd0, qhi = (uint32_t)(qd0 >> 32);
         const uint32_t rlo = (uint32_t)rd0, rhi = (uint32_t)(rd0 >> 32);
         const uint32_t idesc_s = idesc_bf16_f32(128, SA_NB, false, false);
-        for (int j = 0; ok && j < p.nblk; ++j) {
-          // S buffer j % 2 was last read by softmax(j - 2)
-          wc.tag = 2000 + j;
-          if (j >= 2 && !(ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->s_free[j & 1], ((j - 2) >> 1) & 1, wc)))) break;
-          const uint32_t d_s = tmem + (j & 1) * SA_SCOLS;
-          if (j >= 2) adv(SA_NKC);
-          for (int d = 0; d < nkb; ++d) {
-            const uint32_t n = rn;
-            const int slh = rs;
-            if (!(ok = take1(n, slh))) break;
-            adv(1);
-            const uint32_t blo = rlo + (uint32_t)(slh * (SA_SLOT >> 4));
-            const uint32_t alo = qlo + (uint32_t)(d * 512);
-            if (leader) {
+        for (int it = 0; ok && it < n_it; ++it) {
+          // both CTAs' query tiles of this token have landed
+          wc.tag = 4000 + it;
+          if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->q_full, it & 1, wc) &&
+                                                  mbar_wait(&sh->peer_q, it & 1, wc, true))))
+            break;
+          tc_fence_after();
+          for (int j = 0; ok && j < p.nblk; ++j) {
+            const int jg = it * p.nblk + j;  // global block index
+            // S buffer jg % 2 was last read by softmax(jg - 2)
+            wc.tag = 2000 + j;
+            if (jg >= 2 && !(ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->s_free[jg & 1], ((jg - 2) >> 1) & 1, wc)))) break;
+            const uint32_t d_s = tmem + (jg & 1) * SA_SCOLS;
+            if (j >= 2) adv(SA_NKC);
+            for (int d = 0; d < nkb; ++d) {
+              const uint32_t n = rn;
+              const int slh = rs;
+              if (!(ok = take1(n, slh))) break;
+              adv(1);
+              const uint32_t blo = rlo + (uint32_t)(slh * (SA_SLOT >> 4));
+              const uint32_t alo = qlo + (uint32_t)(d * 512);
+              if (leader) {
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                umma_cg2_w(d_s, alo + kk * 2, qhi, blo + kk * 2, rhi, idesc_s, (d > 0 || kk > 0) ? 1u : 0u);
-              umma_commit_cg2(&sh->empty[slh], 3);
+                for (int kk = 0; kk < 4; ++kk)
+                  umma_cg2_w(d_s, alo + kk * 2, qhi, blo + kk * 2, rhi, idesc_s, (d > 0 || kk > 0) ? 1u : 0u);
+                umma_commit_cg2(&sh->empty[slh], 3);
+              }
+              __syncwarp();
+              KS_SA_TRACE(12, n);
             }
+            if (!ok) break;
+            if (leader) umma_commit_cg2(&sh->acc_full[jg & 1], 3);
             __syncwarp();
-            KS_SA_TRACE(12, n);
           }
           if (!ok) break;
-          if (leader) umma_commit_cg2(&sh->acc_full[j & 1], 3);
-          __syncwarp();
+          adv(p.nblk >= 2 ? 2 * SA_NKC : SA_NKC);  // to the next token's S(0)
+          if (it + 1 < n_it) {
+            // the query tiles are free once this token's QK MMAs have completed;
+            // both CTAs then load the next token's
+            if (leader) umma_commit_cg2(&sh->q_free, 3);
+            __syncwarp();
+            if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->q_free, it & 1, wc)))) break;
+            if (lane == 0) {
+              load_q(cid + (int64_t)(it + 1) * ncl);
+              ++q_loads;
+            }
+            __syncwarp();
+          }
         }
         if (leader) umma_commit_cg2(&sh->drain_s, 1);
         __syncwarp();
@@ -392,54 +470,72 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         const uint32_t idesc_pv0 = idesc_bf16_f32(128, p.pv_n[0], false, true);
         const uint32_t idesc_pv1 = idesc_bf16_f32(128, p.n_pv > 1 ? p.pv_n[1] : 128, false, true);
         const int npv = p.n_pv, pvn0 = p.pv_n[0];
-        for (int j = 0; ok && j < p.nblk; ++j) {
-          // P(j) written (and O rescaled) by the softmax
-          wc.tag = 1000 + j;
-          if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->p_full[j & 1], (j >> 1) & 1, wc)))) break;
-          KS_SA_TRACE(8, j);
-          for (int sp = 0; sp < SA_NKC; sp += 2) {
+        for (int it = 0; ok && it < n_it; ++it) {
+          for (int j = 0; ok && j < p.nblk; ++j) {
+            const int jg = it * p.nblk + j;
+            // P(jg) written (and O rescaled) by the softmax; for a token's first
+            // block also the previous token's O read out by the epilogue
+            wc.tag = 1000 + j;
+            if (!(ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->p_full[jg & 1], (jg >> 1) & 1, wc)))) break;
+            KS_SA_TRACE(8, j);
+            for (int sp = 0; sp < SA_NKC; sp += 2) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int sub = sp + h;
-              const uint32_t n = rn;
-              const int slh = rs;
-              if (!(ok = take1(n, slh))) break;
-              adv(1);
-              const uint32_t boff = (uint32_t)(slh * (SA_SLOT >> 4));
-              const uint32_t alo = plo + (uint32_t)((j & 1) * (SA_PBYTES >> 4) + (sub >> 1) * 512 + (sub & 1) * 4);
-              if (leader) {
+              for (int h = 0; h < 2; ++h) {
+                const int sub = sp + h;
+                const uint32_t n = rn;
+                const int slh = rs;
+                if (!(ok = take1(n, slh))) break;
+                adv(1);
+                const uint32_t boff = (uint32_t)(slh * (SA_SLOT >> 4));
+                const uint32_t alo = plo + (uint32_t)((jg & 1) * (SA_PBYTES >> 4) + (sub >> 1) * 512 + (sub & 1) * 4);
+                if (leader) {
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                  if (i == 1 && npv < 2) break;
-                  // instruction i: N = pv_n[i]; its columns start at segment 2 i (pv_n[0] = 256 when there are two)
-                  const uint32_t ocol = tmem + SA_OCOL + (i ? pvn0 / 2 : 0);
-                  const uint32_t blo = rlo + boff + (uint32_t)(i ? (pvn0 / 128) * (SA_VSEG >> 4) : 0);
+                  for (int i = 0; i < 2; ++i) {
+                    if (i == 1 && npv < 2) break;
+                    // instruction i: N = pv_n[i]; its columns start at segment 2 i (pv_n[0] = 256 when there are two)
+                    const uint32_t ocol = tmem + SA_OCOL + (i ? pvn0 / 2 : 0);
+                    const uint32_t blo = rlo + boff + (uint32_t)(i ? (pvn0 / 128) * (SA_VSEG >> 4) : 0);
 #pragma unroll
-                  for (int kk = 0; kk < SA_KC / 16; ++kk)
-                    umma_cg2_w(ocol, alo + kk * 2, phi, blo + kk * 128, rhi, i ? idesc_pv1 : idesc_pv0,
-                               (j > 0 || sub > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < SA_KC / 16; ++kk)
+                      umma_cg2_w(ocol, alo + kk * 2, phi, blo + kk * 128, rhi, i ? idesc_pv1 : idesc_pv0,
+                                 (j > 0 || sub > 0 || kk > 0) ? 1u : 0u);
+                  }
+                  umma_commit_cg2(&sh->empty[slh], 3);
                 }
-                umma_commit_cg2(&sh->empty[slh], 3);
+                __syncwarp();
+                KS_SA_TRACE(12, n);
               }
-              __syncwarp();
-              KS_SA_TRACE(12, n);
+              if (!ok) break;
             }
             if (!ok) break;
+            if (leader) umma_commit_cg2(&sh->p_free[jg & 1], 3);
+            __syncwarp();
+            if (j + 2 < p.nblk) adv(nkb);
           }
           if (!ok) break;
-          if (leader) umma_commit_cg2(&sh->p_free[j & 1], 3);
+          if (leader) umma_commit_cg2(&sh->o_full, 3);
           __syncwarp();
-          if (j + 2 < p.nblk) adv(nkb);
+          adv(s01);  // past the next token's S(0) S(1)
         }
-        if (ok && leader) umma_commit_cg2(&sh->o_full, 3);
         if (leader) umma_commit_cg2(&sh->drain_v, 1);
         __syncwarp();
         mbar_wait(&sh->drain_v, 0, wc, false, true);
       }
     } else if (lane == 0 && warp == SA_MMA_WARP) {
-      // CTA 1: tell the leader that this CTA's query tile has landed
-      if (mbar_wait(&sh->q_full, 0, wc)) mbar_arrive_cluster(&sh->peer_q, 0);
+      // CTA 1: tell the leader that this CTA's query tile has landed; reload it
+      // for the next token once the leader's QK MMAs are done with it
+      for (int it = 0; it < n_it; ++it) {
+        wc.tag = 4000 + it;
+        if (!mbar_wait(&sh->q_full, it & 1, wc)) break;
+        mbar_arrive_cluster(&sh->peer_q, 0);
+        if (it + 1 == n_it) break;
+        if (!mbar_wait(&sh->q_free, it & 1, wc)) break;
+        load_q(cid + (int64_t)(it + 1) * ncl);
+        ++q_loads;
+      }
     }
+    // every query tile load issued has landed before the CTA exits
+    if (warp == SA_MMA_WARP && lane == 0) mbar_wait(&sh->q_full, (q_loads - 1) & 1, wc, false, true);
   } else if (warp >= SA_SMX_WARP0) {
     // ------------------------------------------------------------ softmax + epilogue
     const int q4 = warp & 3;
@@ -451,7 +547,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
     float m_used = sink2, lsum = 0.f;
     const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
     const int o_cols = p.dv_pad / 2;
-    bool oob = false;  // an index >= N was seen (reported once, after the last block)
+    const int32_t* ip = p.idx;  // the current token's index row
+    bool oob = false;  // an index >= N was seen (reported once per token, after its last block)
     // validity bits of this lane's 128 keys of block j (warp-uniform loads).  An
     // index >= N (which the reference's gather rejects) is masked like -1 and, in
     // CTA 0, reported as a bounds error; negative indices are masked silently.
@@ -486,12 +583,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       }
     };
     bool ok = true;
+    for (int it = 0; ok && it < n_it; ++it) {
+    const int64_t token = cid + (int64_t)it * ncl;
+    ip = p.idx + token * p.K;
+    m_used = sink2;
+    lsum = 0.f;
+    oob = false;
     for (int j = 0; j < p.nblk; ++j) {
-      const int sb = j & 1;
+      const int jg = it * p.nblk + j;  // global block index (barrier phases, S and P buffers)
+      const int sb = jg & 1;
       uint32_t mk[4];
       valid_bits(j, mk);
       wc.tag = 3000 + j;
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->acc_full[sb], (j >> 1) & 1, wc));
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->acc_full[sb], (jg >> 1) & 1, wc));
       if (!ok) break;
       tc_fence_after();
       if (l == 0) KS_SA_TRACE(9, j);
@@ -523,11 +627,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       }
       bmax = (sgn * bmax) * p.scale_log2;  // -inf when no key is valid
       // block max of the head = max over this lane and its partner (lane l ^ 64)
-      sh->xslot[j & 1][l] = bmax;
-      mbar_arrive(&sh->xchg[j & 1]);
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->xchg[j & 1], (j >> 1) & 1, wc));
+      sh->xslot[sb][l] = bmax;
+      mbar_arrive(&sh->xchg[sb]);
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->xchg[sb], (jg >> 1) & 1, wc));
       if (!ok) break;
-      const float m_new = fmaxf(m_used, fmaxf(bmax, sh->xslot[j & 1][l ^ 64]));
+      const float m_new = fmaxf(m_used, fmaxf(bmax, sh->xslot[sb][l ^ 64]));
       const bool resc = m_new > m_used + 8.f;
       float alpha = 1.f;
       if (resc) {
@@ -535,14 +639,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         lsum *= alpha;
         m_used = m_new;
       }
-      // P is double buffered: P(j) goes to buffer j % 2, last read by PV(j - 2)
-      if (j >= 2) {
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->p_free[j & 1], ((j - 2) >> 1) & 1, wc));
+      // P is double buffered: P(jg) goes to buffer jg % 2, last read by PV(jg - 2)
+      if (jg >= 2) {
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->p_free[sb], ((jg - 2) >> 1) & 1, wc));
         if (!ok) break;
       }
+      // (a token's first PV overwrites O, so O holds nothing to rescale at j = 0)
       if (j >= 1 && __any_sync(0xFFFFFFFFu, resc)) {  // TMEM access is warp-wide; alpha = 1 elsewhere
-        // O is rescaled once PV(j - 1) has finished with it
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, wc));
+        // O is rescaled once PV(jg - 1) has finished with it
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait_inl(&sh->p_free[(jg - 1) & 1], ((jg - 1) >> 1) & 1, wc));
         if (!ok) break;
         {
           tc_fence_after();
@@ -564,7 +669,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       {
         const float neg_m = -m_used;
         float ls0 = 0.f, ls1 = 0.f;
-        uint8_t* pbase = ps + (j & 1) * SA_PBYTES + (2 * half) * 8192 + m * 128;
+        uint8_t* pbase = ps + sb * SA_PBYTES + (2 * half) * 8192 + m * 128;
 #pragma unroll
         for (int c16 = 0; c16 < 8; ++c16) {
           uint32_t r[16];
@@ -593,7 +698,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         lsum += ls0 + ls1;
       }
       tc_fence_before();
-      sa_warp_ready(&sh->p_full[j & 1], cta, lane);
+      sa_warp_ready(&sh->p_full[sb], cta, lane);
       if (lane == 0) {  // S buffer sb read out
         if (cta == 0) mbar_arrive(&sh->s_free[sb]);
         else mbar_arrive_cluster(&sh->s_free[sb], 0);
@@ -601,14 +706,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
       if (lane == 0) KS_SA_TRACE(11, 16 * q4 + j);
     }
     if (cta == 0 && __any_sync(0xFFFFFFFFu, oob) && oob) report_bounds(p.status, (int)token, p.N);
-    if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->o_full, 0, wc));
-    // tail: the last two "P free" signals land before the CTA exits (see the gathers)
-    for (int jj = p.nblk - 2; ok && jj < p.nblk; ++jj)
-      if (jj >= 0) mbar_wait(&sh->p_free[jj & 1], (jj >> 1) & 1, wc, false, true);
+    if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->o_full, it & 1, wc));
     if (ok) {
       sh->xslot[2][l] = lsum;
       mbar_arrive(&sh->xchg[2]);
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->xchg[2], 0, wc));
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->xchg[2], it & 1, wc));
     }
     if (ok) {
       tc_fence_after();
@@ -636,6 +738,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
         ocol += hn;
       }
     }
+    }  // tokens
+    // tail: the last two "P free" signals land before the CTA exits (see the gathers)
+    const int jtot = n_it * p.nblk;
+    for (int jj = jtot - 2; ok && jj < jtot; ++jj)
+      if (jj >= 0) mbar_wait(&sh->p_free[jj & 1], (jj >> 1) & 1, wc, false, true);
   }
 
   tc_fence_before();
