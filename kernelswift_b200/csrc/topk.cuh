@@ -67,6 +67,35 @@ __device__ __forceinline__ uint32_t bf16_key(uint32_t u) {
   if (u == 0x8000u) u = 0;  // -0.0 == +0.0
   return (u & 0x8000u) ? ((~u) & 0xFFFFu) : (u | 0x8000u);
 }
+// bf16_key of both halves of a word: a negative half is inverted (xor 0xFFFF), a
+// non-negative one gets its sign bit set (xor 0x8000).  m - (m >> 15) turns each
+// half's sign bit into 0x7FFF without a borrow between the halves.  -0.0 halves
+// must have been folded onto +0.0 first (fold_negzero2).
+__device__ __forceinline__ uint32_t bf16_key2(uint32_t w) {
+  const uint32_t m = w & 0x80008000u;
+  return w ^ (0x80008000u | (m - (m >> 15)));
+}
+// Nonzero when some half of w may be 0x8000 (-0.0): the zero-half test on w ^ 0x8000
+// per half (it can also fire for other words; fold_negzero2 then changes nothing).
+__device__ __forceinline__ uint32_t maybe_negzero2(uint32_t w) {
+  const uint32_t t = w ^ 0x80008000u;
+  return (t - 0x00010001u) & ~t & 0x80008000u;
+}
+__device__ __forceinline__ uint32_t fold_negzero2(uint32_t w) {
+  if ((w >> 16) == 0x8000u) w &= 0x0000FFFFu;
+  if ((w & 0xFFFFu) == 0x8000u) w &= 0xFFFF0000u;
+  return w;
+}
+__device__ __forceinline__ uint32_t min_u16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("min.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
 
 // Exclusive scan of one value per thread over the block; also returns the total.
 __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* warp_tot,
@@ -151,28 +180,25 @@ __global__ void __launch_bounds__(TK_THREADS, 3) topk_rows_kernel(TopkParams p) 
   // ---- stage the valid prefix as order keys; smallest and largest key
   const bool need_select = L > K;
   uint32_t kmin = 0xFFFFu, kmax = 0u;
+  uint32_t kmin2 = 0xFFFFFFFFu, kmax2 = 0u;  // per half, full chunks (two keys per word)
   for (int base = 0; base < L; base += TK_CHUNK) {
     const int i0 = base + tid * TK_PER_THREAD;
     uint32_t kv[TK_PER_THREAD];
     if (i0 + TK_PER_THREAD <= L) {
       const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src + i0));
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      // order keys two per word; -0.0 is rare, so one test covers the 8 values
+      if (maybe_negzero2(w[0]) | maybe_negzero2(w[1]) | maybe_negzero2(w[2]) | maybe_negzero2(w[3])) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) w[q] = fold_negzero2(w[q]);
+      }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        kv[2 * q] = bf16_key(w[q] & 0xFFFFu);
-        kv[2 * q + 1] = bf16_key(w[q] >> 16);
+        w[q] = bf16_key2(w[q]);
+        kmin2 = min_u16x2(kmin2, w[q]);
+        kmax2 = max_u16x2(kmax2, w[q]);
       }
-      uint4 o;
-      o.x = kv[0] | (kv[1] << 16);
-      o.y = kv[2] | (kv[3] << 16);
-      o.z = kv[4] | (kv[5] << 16);
-      o.w = kv[6] | (kv[7] << 16);
-      *reinterpret_cast<uint4*>(keys + i0) = o;
-#pragma unroll
-      for (int q = 0; q < TK_PER_THREAD; ++q) {
-        kmin = min(kmin, kv[q]);
-        kmax = max(kmax, kv[q]);
-      }
+      *reinterpret_cast<uint4*>(keys + i0) = make_uint4(w[0], w[1], w[2], w[3]);
     } else {
 #pragma unroll
       for (int q = 0; q < TK_PER_THREAD; ++q) {
@@ -186,6 +212,8 @@ __global__ void __launch_bounds__(TK_THREADS, 3) topk_rows_kernel(TopkParams p) 
     }
   }
 
+  kmin = min(kmin, min(kmin2 & 0xFFFFu, kmin2 >> 16));
+  kmax = max(kmax, max(kmax2 & 0xFFFFu, kmax2 >> 16));
   // the row's smallest and largest key (for the threshold bins and the counting sort)
   const int lane = tid & 31, warp = tid >> 5;
   if (need_select) {
@@ -211,6 +239,7 @@ __global__ void __launch_bounds__(TK_THREADS, 3) topk_rows_kernel(TopkParams p) 
     const uint32_t range = kmax - kmin;
     const int bits = range ? 32 - __clz(range) : 0;
     const int sh = bits > TK_HBITS ? bits - TK_HBITS : 0;
+    const uint32_t kmin2w = kmin | (kmin << 16);
     for (int base = 0; base < L; base += TK_CHUNK) {
       const int i0 = base + tid * TK_PER_THREAD;
       if (i0 + TK_PER_THREAD <= L) {
@@ -218,8 +247,9 @@ __global__ void __launch_bounds__(TK_THREADS, 3) topk_rows_kernel(TopkParams p) 
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          atomicAdd(hist + (((w[q] & 0xFFFFu) - kmin) >> sh), 1u);
-          atomicAdd(hist + (((w[q] >> 16) - kmin) >> sh), 1u);
+          const uint32_t d = w[q] - kmin2w;  // both halves at once: no half is below kmin
+          atomicAdd(hist + ((d & 0xFFFFu) >> sh), 1u);
+          atomicAdd(hist + (d >> (16 + sh)), 1u);
         }
       } else {
         for (int q = 0; q < TK_PER_THREAD; ++q)
