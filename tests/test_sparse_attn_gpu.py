@@ -196,3 +196,25 @@ def test_out_of_range_index_reported(cuda_ok):
     # in-range calls leave the status clean
     ops.sparse_attn(q.cuda(), kv.cuda(), s.cuda(), idx.cuda(), D ** -0.5)
     ops.device_status()
+
+
+@pytest.mark.parametrize("K", [100, 300, 700])  # one, two and three 256-key blocks
+def test_persistent_token_sequences(cuda_ok, K):
+    """More tokens than resident CTA pairs (300 tokens over at most 74 pairs), so each
+    pair runs several tokens in a row with the ring, barrier phases and S / P buffers
+    carried across them.  Block counts 1, 2 and 3 take the three ring layouts at a
+    token boundary; duplicates, -1 entries and fully masked rows check that no
+    running max, sum or output leaks from one token into the next."""
+    from kernelswift_b200 import ops
+
+    B, M, H, D, N, dv = 2, 150, 128, 128, 2000, 128
+    q, kv, s, idx = make_case(B, M, H, D, N, K, seed=31 + K, mode="mixed")
+    idx[0, 7] = -1          # nothing valid
+    idx[1, 80, 1:] = -1     # a single valid key
+    idx[1, 149] = 17        # one key repeated K times
+    out = ops.sparse_attn(q.cuda(), kv.cuda(), s.cuda(), idx.cuda(), D ** -0.5, dv)
+    ops.device_status()
+    ref = O.sparse_attn(bits_from_bf16(q), bits_from_bf16(kv), s.numpy(), idx.numpy(), D ** -0.5, dv)
+    assert_close(bits_from_bf16(out), ref)
+    again = ops.sparse_attn(q.cuda(), kv.cuda(), s.cuda(), idx.cuda(), D ** -0.5, dv)
+    assert torch.equal(out, again)
