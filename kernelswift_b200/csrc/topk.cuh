@@ -181,11 +181,18 @@ __global__ void __launch_bounds__(TK_THREADS, 3) topk_rows_kernel(TopkParams p) 
   const bool need_select = L > K;
   uint32_t kmin = 0xFFFFu, kmax = 0u;
   uint32_t kmin2 = 0xFFFFFFFFu, kmax2 = 0u;  // per half, full chunks (two keys per word)
+  // the next chunk's 16 bytes are loaded while this chunk is converted, so the
+  // loop does not wait out one memory latency per 8 keys
+  uint4 nxt = make_uint4(0u, 0u, 0u, 0u);
+  if (tid * TK_PER_THREAD + TK_PER_THREAD <= L)
+    nxt = __ldcs(reinterpret_cast<const uint4*>(src + tid * TK_PER_THREAD));
   for (int base = 0; base < L; base += TK_CHUNK) {
     const int i0 = base + tid * TK_PER_THREAD;
     uint32_t kv[TK_PER_THREAD];
+    const uint4 v = nxt;
+    if (i0 + TK_CHUNK + TK_PER_THREAD <= L)
+      nxt = __ldcs(reinterpret_cast<const uint4*>(src + i0 + TK_CHUNK));
     if (i0 + TK_PER_THREAD <= L) {
-      const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src + i0));
       uint32_t w[4] = {v.x, v.y, v.z, v.w};
       // order keys two per word; -0.0 is rare, so one test covers the 8 values
       if (maybe_negzero2(w[0]) | maybe_negzero2(w[1]) | maybe_negzero2(w[2]) | maybe_negzero2(w[3])) {
