@@ -19,6 +19,7 @@
 #include "sparse_attn.cuh"
 #include "sparse_attn_small.cuh"
 #include "topk.cuh"
+#include "topk_small.cuh"
 
 namespace ks {
 
@@ -309,6 +310,19 @@ int topk_impl(const void* scores, int64_t score_ld, int64_t B, int64_t S, int64_
   p.kpow2 = kpow2;
   p.status = dev->status;
   if (B * S > 0x7FFFFFFFll) return fail(KS_ERR_UNSUPPORTED, "topk: too many rows");
+  // short rows and small k: one warp per row (topk_small.cuh)
+  if (T <= TS_MAXT && kpow2 <= 256) {
+    const int epl = kpow2 <= 32 ? 1 : kpow2 / 32;
+    const size_t smem_s = (size_t)TS_WARPS * ((size_t)TS_MAXT * 2 + (size_t)32 * epl * 4);  // <= 40 KB
+    const unsigned blocks = (unsigned)((B * S + TS_WARPS - 1) / TS_WARPS);
+    switch (epl) {
+      case 1: topk_small_kernel<1><<<blocks, TS_WARPS * 32, smem_s, st>>>(p); break;
+      case 2: topk_small_kernel<2><<<blocks, TS_WARPS * 32, smem_s, st>>>(p); break;
+      case 4: topk_small_kernel<4><<<blocks, TS_WARPS * 32, smem_s, st>>>(p); break;
+      default: topk_small_kernel<8><<<blocks, TS_WARPS * 32, smem_s, st>>>(p); break;
+    }
+    return launch_check("topk_small_kernel launch");
+  }
   // composites sorted per row: TK_THREADS * ept >= kpow2
   const int ept = kpow2 <= TK_THREADS ? 1 : kpow2 / TK_THREADS;
   const size_t nbuf = (size_t)TK_THREADS * ept > (size_t)TK_HBINS ? (size_t)TK_THREADS * ept : (size_t)TK_HBINS;

@@ -30,6 +30,11 @@ CASES = [
     (3, 17, 65, 16, 1, True, 0, 0, 1),                # T not a multiple of 8
     (1, 8, 40000, 4096, 1, False, 0, 0, None),        # k = 4096, long rows
     (1, 4, 65536, 2048, 1, False, 0, 0, 8),           # maximum T
+    # the one-warp-per-row path (T <= 2048, k <= 256) and its edges
+    (2, 40, 2048, 256, 1, True, 3, 2000, 2),          # longest warp-path rows, ties
+    (1, 40, 2049, 256, 1, False, 0, 0, None),         # one key past it: row kernel
+    (1, 40, 1000, 257, 1, False, 0, 0, 4),            # k past it: row kernel
+    (4, 33, 513, 33, 1, False, 9, 0, 1),              # k = 33 (64-wide sort), coarse ties
 ]
 
 
