@@ -226,23 +226,37 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
             __syncwarp();
           }
           uint32_t o[8];
-          const int d0 = (tn * p.n_tile + c) % p.hd;  // head-local column of r[16 h]
+          // head-local column of r[16 h]; a 16-column step never crosses a head (hd
+          // and the tile's columns are multiples of 16), so it is wholly rotated or
+          // not, unless rope0 falls inside it.  (Rows past M rotate with row 0's
+          // factors; the TMA store clips them.)
+          const int dc = tn * p.n_tile + c;
+          const int d0 = (p.hd & (p.hd - 1)) == 0 ? dc & (p.hd - 1) : dc % p.hd;
+          const bool all_rot = p.rd > 0 && d0 >= rope0;
+          const bool some_rot = p.rd > 0 && d0 + 16 > rope0;
+          auto rotate = [&](uint32_t v, int j) -> uint32_t {
+            const float2 cs = reinterpret_cast<const float2*>(my_fr)[j];
+            const float xr = bf16lo_f32(v), xi = bf16hi_f32(v);
+            const float re = __fsub_rn(__fmul_rn(xr, cs.x), __fmul_rn(xi, cs.y));
+            const float im = __fadd_rn(__fmul_rn(xr, cs.y), __fmul_rn(xi, cs.x));
+            return cvt_bf16x2(re, im);
+          };
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            // bf16 rounding of the GEMM output (F.linear returns bf16)
-            uint32_t v = cvt_bf16x2(__uint_as_float(r[16 * h + 2 * i]), __uint_as_float(r[16 * h + 2 * i + 1]));
-            const int d = d0 + 2 * i;
-            if (p.rd > 0 && d >= rope0 && row_ok) {
-              const int j = (d - rope0) >> 1;
-              const float2 cs = reinterpret_cast<const float2*>(my_fr)[j];
-              const float xr = bf16lo_f32(v), xi = bf16hi_f32(v);
-              const float re = __fsub_rn(__fmul_rn(xr, cs.x), __fmul_rn(xi, cs.y));
-              const float im = __fadd_rn(__fmul_rn(xr, cs.y), __fmul_rn(xi, cs.x));
-              v = cvt_bf16x2(re, im);
-            }
-            if (p.apply_scale)
-              v = cvt_bf16x2(__fmul_rn(bf16lo_f32(v), p.scale), __fmul_rn(bf16hi_f32(v), p.scale));
-            o[i] = v;
+          for (int i = 0; i < 8; ++i)  // bf16 rounding of the GEMM output (F.linear returns bf16)
+            o[i] = cvt_bf16x2(__uint_as_float(r[16 * h + 2 * i]), __uint_as_float(r[16 * h + 2 * i + 1]));
+          if (all_rot) {
+            const int j0 = (d0 - rope0) >> 1;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = rotate(o[i], j0 + i);
+          } else if (some_rot) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              if (d0 + 2 * i >= rope0) o[i] = rotate(o[i], (d0 + 2 * i - rope0) >> 1);
+          }
+          if (p.apply_scale) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              o[i] = cvt_bf16x2(__fmul_rn(bf16lo_f32(o[i]), p.scale), __fmul_rn(bf16hi_f32(o[i]), p.scale));
           }
           if (p.tma_store) {
             // row `lane` of the box, 16-byte units 2 s and 2 s + 1 (s = the 16-column
