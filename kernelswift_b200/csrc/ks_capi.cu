@@ -680,7 +680,15 @@ int ks_proj_rope(const void* a, const void* w, void* out, int64_t M, int64_t N, 
   // output through TMA stores (boxes of 64 columns) when a tile is at least that wide
   p.tma_store = n_tile >= 64 ? 1 : 0;
   const size_t out_stage = p.tma_store ? 32768 : 0;
-  int stages = (int)((232448 - 2048 - fr_bytes - out_stage) / st_bytes);
+  // Tiles at most 64 columns wide need at most 2 x 64 TMEM columns: two CTAs share
+  // an SM (half the shared memory each) when that still leaves three ring stages,
+  // so a short grid (e.g. N = 16: 163 tiles on 148 SMs) runs in one wave.
+  const size_t two_budget = 112 * 1024;
+  const bool two_per_sm = n_tile <= 64 && (int)((two_budget - 2048 - fr_bytes - out_stage) / st_bytes) >= 3;
+  const size_t budget = two_per_sm ? two_budget : 232448;
+  p.acc_cols = n_tile >= 128 ? 256u : (n_tile < 32 ? 32u : (uint32_t)n_tile);
+  p.tmem_cols = 2 * p.acc_cols;
+  int stages = (int)((budget - 2048 - fr_bytes - out_stage) / st_bytes);
   if (stages > PG_MAX_STAGES) stages = PG_MAX_STAGES;
   if (stages < 2) return fail(KS_ERR_UNSUPPORTED, "proj_rope: shared memory too small");
   p.stages = stages;
@@ -690,10 +698,10 @@ int ks_proj_rope(const void* a, const void* w, void* out, int64_t M, int64_t N, 
   p.tiles_n = (int)(N / n_tile);
   p.status = dev->status;
   p.budget_ns = wait_budget_ns();
-  // at least half of the shared memory, so two CTAs never share an SM (each
-  // allocates all 512 TMEM columns)
+  // one CTA per SM takes at least half of the shared memory, so two never share an
+  // SM (each allocates all 512 TMEM columns)
   size_t smem = 1024 + 1024 + (size_t)stages * st_bytes + fr_bytes + out_stage;
-  if (smem < 120 * 1024) smem = 120 * 1024;
+  if (!two_per_sm && smem < 120 * 1024) smem = 120 * 1024;
   CUtensorMap am, bm, om;
   if (int rc = make_map_bf16(&am, a, K, (uint64_t)M, K * 2, 64, PG_TILE_M)) return rc;
   if (int rc = make_map_bf16(&bm, w, K, (uint64_t)N, K * 2, 64, n_tile)) return rc;
@@ -702,12 +710,16 @@ int ks_proj_rope(const void* a, const void* w, void* out, int64_t M, int64_t N, 
   } else {
     om = am;  // unused
   }
-  if (int rc = smem_optin(dev, reinterpret_cast<const void*>(proj_gemm_kernel),
-                          "cudaFuncSetAttribute(proj_gemm)"))
-    return rc;
+  const void* pfn = two_per_sm ? reinterpret_cast<const void*>(proj_gemm_kernel<PG_THREADS_NARROW, 2>)
+                               : reinterpret_cast<const void*>(proj_gemm_kernel<PG_THREADS, 1>);
+  if (int rc = smem_optin(dev, pfn, "cudaFuncSetAttribute(proj_gemm)")) return rc;
   const int64_t tiles = (int64_t)p.tiles_m * p.tiles_n;
-  const int grid = (int)(tiles < dev->num_sms ? tiles : dev->num_sms);
-  proj_gemm_kernel<<<grid, PG_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(am, bm, om, p);
+  const int64_t slots = (int64_t)dev->num_sms * (two_per_sm ? 2 : 1);
+  const int grid = (int)(tiles < slots ? tiles : slots);
+  if (two_per_sm)
+    proj_gemm_kernel<PG_THREADS_NARROW, 2><<<grid, PG_THREADS_NARROW, smem, static_cast<cudaStream_t>(stream)>>>(am, bm, om, p);
+  else
+    proj_gemm_kernel<PG_THREADS, 1><<<grid, PG_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(am, bm, om, p);
   return launch_check("proj_gemm_kernel launch");
 }
 

@@ -13,7 +13,7 @@
 // (16 MB for 64 heads x 128 dims x 1024) from L2; as its producer the GEMM reads
 // each operand tile once per output tile.
 //
-// One persistent CTA per SM, 10 warps: warp 0 TMA producer (A tile 128 x 64 and
+// Persistent CTAs (one per SM; two for tiles at most 64 columns wide), 10 warps: warp 0 TMA producer (A tile 128 x 64 and
 // B tile N_TILE x 64 per stage, 128-byte swizzle), warp 1 TMEM owner and MMA
 // issuer (M = 128, N = N_TILE, K = 16 per instruction, fp32 accumulators double
 // buffered in TMEM), warps 2-9 epilogue: thread = output row = TMEM lane, two
@@ -25,6 +25,7 @@
 namespace ks {
 
 constexpr int PG_THREADS = 320;
+constexpr int PG_THREADS_NARROW = 192;
 constexpr int PG_EPI_WARP0 = 2;
 constexpr int PG_EPI_WARPS = 8;
 constexpr int PG_TILE_M = 128;
@@ -43,6 +44,8 @@ struct ProjParams {
   uint32_t fr_off;      // shared-memory offset of the per-row RoPE factors (rd > 0)
   uint32_t st_off;      // shared-memory offset of the output staging boxes (tma_store)
   int32_t tma_store;    // write the output through TMA stores (n_tile >= 64)
+  uint32_t acc_cols;    // TMEM columns per accumulator buffer (two buffers)
+  uint32_t tmem_cols;   // TMEM columns allocated (2 acc_cols, a power of two >= 32)
   int* status;
   uint64_t budget_ns;
 };
@@ -57,7 +60,10 @@ struct PgShared {
 };
 static_assert(sizeof(PgShared) <= 1024, "PgShared exceeds its header");
 
-__global__ void __launch_bounds__(PG_THREADS, 1)
+// THREADS = PG_THREADS (one CTA per SM) or PG_THREADS_NARROW (tiles at most 64
+// columns wide: four epilogue warps, two CTAs per SM within the register file)
+template <int THREADS, int MIN_BLOCKS>
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS)
     proj_gemm_kernel(const __grid_constant__ CUtensorMap amap,
                      const __grid_constant__ CUtensorMap bmap,
                      const __grid_constant__ CUtensorMap omap, ProjParams p) {
@@ -95,7 +101,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc<1>(&sh->tmem_base, 512);
+    tmem_alloc<1>(&sh->tmem_base, p.tmem_cols);
     tmem_relinquish<1>();
   }
   tc_fence_before();
@@ -135,7 +141,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
         const int as = ac & 1;
         if (!(ok = mbar_wait(&sh->acc_empty[as], ((ac >> 1) & 1) ^ 1, wc))) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + as * 256;
+        const uint32_t d_tmem = tmem + as * p.acc_cols;
         for (int kc = 0; kc < n_k; ++kc, ++c) {
           const int st = (int)(c % (uint32_t)p.stages);
           if (!(ok = mbar_wait_inl(&sh->full[st], (c / p.stages) & 1, wc))) break;
@@ -203,7 +209,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
         }
       }
       uint16_t* orow = p.out + (int64_t)m * p.N + (int64_t)tn * p.n_tile;
-      const uint32_t tbase = tmem + as * 256 + ((uint32_t)(quarter * 32) << 16);
+      const uint32_t tbase = tmem + as * p.acc_cols + ((uint32_t)(quarter * 32) << 16);
       uint8_t* box = stage;
       // 32 columns per TMEM load where the range allows, one wait per load
       for (int c0 = c_begin; c0 < c_end; c0 += 32) {
@@ -292,7 +298,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc<1>(tmem, 512);
+  if (warp == 1) tmem_dealloc<1>(tmem, p.tmem_cols);
 }
 
 }  // namespace ks
