@@ -51,7 +51,7 @@ struct Device {
   int num_sms = 0;
   // kernels whose dynamic shared-memory opt-in has been set on this device
   // (cudaFuncSetAttribute acts on the current device's context only)
-  const void* smem_optin[16] = {};
+  const void* smem_optin[64] = {};  // more than the library's kernel instances
   int n_smem_optin = 0;
   // co-resident CTA pairs of the persistent attention kernel, for the shared
   // memory size it was last asked for
@@ -88,9 +88,9 @@ int smem_optin(Device* d, const void* func, const char* what) {
     if (d->smem_optin[i] == func) return KS_OK;
   cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
   if (e != cudaSuccess) return cuda_fail(e, what);
-  if (d->n_smem_optin >= (int)(sizeof(d->smem_optin) / sizeof(d->smem_optin[0])))
-    return fail(KS_ERR_UNSUPPORTED, "too many kernels with a shared-memory opt-in");
-  d->smem_optin[d->n_smem_optin++] = func;
+  // the table only saves repeating the call: when it is full the attribute is set anyway
+  if (d->n_smem_optin < (int)(sizeof(d->smem_optin) / sizeof(d->smem_optin[0])))
+    d->smem_optin[d->n_smem_optin++] = func;
   return KS_OK;
 }
 
