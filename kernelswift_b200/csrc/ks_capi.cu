@@ -18,6 +18,7 @@
 #include "sinkhorn.cuh"
 #include "sparse_attn.cuh"
 #include "sparse_attn_small.cuh"
+#include "sparse_attn_tiny.cuh"
 #include "topk.cuh"
 #include "topk_small.cuh"
 
@@ -353,6 +354,42 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
   if (B * M * H >= (1ll << 31) || B * N >= (1ll << 31) || 2 * B * M >= (1ll << 31))
     return fail(KS_ERR_UNSUPPORTED, "sparse_attn: too many rows");
   if (M == 0) return KS_OK;
+  // Very short index rows: 128 / H tokens per 128-row tile, heads as the MMA's M
+  // dimension (sparse_attn_tiny.cuh).
+  if (H >= 16 && 128 % H == 0 && K <= SAT_MAX_K && D <= 256 && dv <= 256 && dv % 64 == 0) {
+    const int tpt = (int)(128 / H);
+    const int kp = (int)round_up(K, 16);
+    const int ncol = tpt * kp;
+    if (ncol <= SAT_MAX_N) {
+      SaTinyParams tp{};
+      tp.q = static_cast<const uint16_t*>(q);
+      tp.idx = idx;
+      tp.kv = static_cast<const uint16_t*>(kv);
+      tp.sink = sink;
+      tp.out = static_cast<uint16_t*>(out);
+      tp.B = (int)B; tp.M = (int)M; tp.H = (int)H; tp.D = (int)D; tp.N = (int)N; tp.K = (int)K;
+      tp.dv_begin = (int)dv_begin; tp.dv = (int)dv;
+      tp.tpt = tpt; tp.kp = kp; tp.ncol = ncol;
+      tp.nkb = (int)(D / 64);
+      const size_t kg_bytes = (size_t)tp.nkb * ncol * 128;          // a multiple of 1 KB
+      const int q_chunks = std::max(tp.nkb, (ncol + 63) / 64);      // Q, then P
+      tp.kg_off = SAT_HDR;
+      tp.q_off = (uint32_t)(SAT_HDR + kg_bytes);
+      int tcols = 32;
+      while (tcols < std::max(ncol, (int)dv)) tcols <<= 1;
+      tp.tmem_cols = (uint32_t)tcols;
+      tp.scale_log2 = scale * 1.4426950408889634f;
+      tp.status = dev->status;
+      tp.budget_ns = wait_budget_ns();
+      const size_t smem = 1024 + SAT_HDR + kg_bytes + (size_t)q_chunks * 16384;
+      if (int rc = smem_optin(dev, reinterpret_cast<const void*>(sparse_attn_tiny_kernel),
+                              "cudaFuncSetAttribute(sparse_attn_tiny)"))
+        return rc;
+      const unsigned grid = (unsigned)((B * M + tpt - 1) / tpt);
+      sparse_attn_tiny_kernel<<<grid, SAT_THREADS, smem, st>>>(tp);
+      return launch_check("sparse_attn_tiny_kernel launch");
+    }
+  }
   // Few heads and short index rows: one CTA per token, keys as the MMA's M
   // dimension (sparse_attn_small.cuh).
   {

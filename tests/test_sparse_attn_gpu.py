@@ -218,3 +218,28 @@ def test_persistent_token_sequences(cuda_ok, K):
     assert_close(bits_from_bf16(out), ref)
     again = ops.sparse_attn(q.cuda(), kv.cuda(), s.cuda(), idx.cuda(), D ** -0.5, dv)
     assert torch.equal(out, again)
+
+
+@pytest.mark.parametrize("B,M,H,D,N,K,dv_begin,dv", [
+    (3, 13, 16, 128, 500, 32, 0, 128),    # 8 tokens per tile, tiles across batches
+    (2, 9, 32, 256, 300, 20, 64, 192),    # 4 tokens per tile, a column slice
+    (1, 7, 128, 256, 777, 64, 0, 256),    # one token per tile, the longest rows
+])
+def test_tiny_rows(cuda_ok, B, M, H, D, N, K, dv_begin, dv):
+    """Index rows of at most 64 keys: 128 / H tokens share one 128-row tile, each
+    row keeping its own token's keys.  Duplicates, -1 entries, fully masked rows
+    and output column slices against the oracle."""
+    from kernelswift_b200 import _lib, ops
+
+    q, kv, s, idx = make_case(B, M, H, D, N, K, seed=41 + H + K, mode="mixed")
+    idx[0, 1] = -1
+    idx[-1, -1, 1:] = idx[-1, -1, 0]
+    out = torch.empty(B, M, H, dv, dtype=torch.bfloat16, device="cuda")
+    qc, kvc, sc, ic = q.cuda(), kv.cuda(), s.cuda(), idx.cuda()
+    _lib.check(_lib.lib().ks_sparse_attn(qc.data_ptr(), kvc.data_ptr(), sc.data_ptr(), ic.data_ptr(),
+                                    out.data_ptr(), B, M, H, D, N, K, dv_begin, dv, D ** -0.5,
+                                    torch.cuda.current_stream().cuda_stream), "ks_sparse_attn")
+    ops.device_status()
+    ref = O.sparse_attn(bits_from_bf16(q), bits_from_bf16(kv), s.numpy(), idx.numpy(), D ** -0.5,
+                        dv_begin + dv)[..., dv_begin:]
+    assert_close(bits_from_bf16(out), ref)
