@@ -379,6 +379,7 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
       while (tcols < std::max(ncol, (int)dv)) tcols <<= 1;
       tp.tmem_cols = (uint32_t)tcols;
       tp.scale_log2 = scale * 1.4426950408889634f;
+      tp.out_v8 = aligned(out, 32) ? 1 : 0;  // rows are dv * 2 bytes, a multiple of 128
       tp.status = dev->status;
       tp.budget_ns = wait_budget_ns();
       const size_t smem = 1024 + SAT_HDR + kg_bytes + (size_t)q_chunks * 16384;

@@ -45,6 +45,7 @@ struct SaTinyParams {
   uint32_t kg_off, q_off; // shared-memory regions (bytes from the aligned base)
   uint32_t tmem_cols;
   float scale_log2;
+  int32_t out_v8;       // out is 32-byte aligned: 32-byte row stores
   int* status;
   uint64_t budget_ns;
 };
@@ -75,6 +76,17 @@ __global__ void __launch_bounds__(SAT_THREADS)
   const uint32_t chunk = (uint32_t)p.ncol * 128u;    // bytes of one 64-dim chunk of kg
   WaitCtx wc{&sh->abort, p.status, p.budget_ns};
 
+  // the index rows of the tile's tokens (-1 for slots past K and tokens past the
+  // end), loaded before the set-up so their latency overlaps it; every copy then
+  // reads its row from shared memory (ncol <= 2 x 128)
+  int32_t ix[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int c = threadIdx.x + u * SAT_THREADS;
+    const int j = c / p.kp, i = c - j * p.kp;
+    const int64_t tok = tok0 + j;
+    ix[u] = (c < p.ncol && i < p.K && tok < n_tok) ? __ldg(p.idx + tok * p.K + i) : -1;
+  }
   if (threadIdx.x == 0) {
     mbar_init(&sh->mma_bar, 1);
     sh->abort = 0;
@@ -85,13 +97,9 @@ __global__ void __launch_bounds__(SAT_THREADS)
     tmem_alloc<1>(&sh->tmem_base, p.tmem_cols);
     tmem_relinquish<1>();
   }
-  // the index rows of the tile's tokens (-1 for slots past K and tokens past the
-  // end), then every copy reads its row from shared memory
-  for (int c = threadIdx.x; c < p.ncol; c += SAT_THREADS) {
-    const int j = c / p.kp, i = c - j * p.kp;
-    const int64_t tok = tok0 + j;
-    sh->idx[c] = (i < p.K && tok < n_tok) ? __ldg(p.idx + tok * p.K + i) : -1;
-  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u)
+    if (threadIdx.x + u * SAT_THREADS < p.ncol) sh->idx[threadIdx.x + u * SAT_THREADS] = ix[u];
   for (int j = threadIdx.x; j < p.tpt; j += SAT_THREADS) {
     const int64_t tok = tok0 + j;
     sh->bat[j] = tok < n_tok ? (int)(tok / p.M) : 0;
@@ -229,9 +237,16 @@ __global__ void __launch_bounds__(SAT_THREADS)
       for (int t = 0; t < 8; ++t)
         w[t] = cvt_bf16x2(__uint_as_float(o[2 * t]) * inv, __uint_as_float(o[2 * t + 1]) * inv);
       if (live) {
-        uint4* dst = reinterpret_cast<uint4*>(orow + cc);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        if (p.out_v8) {  // one whole 32-byte sector per store
+          asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(orow + cc),
+                       "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]),
+                       "r"(w[7])
+                       : "memory");
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(orow + cc);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
       }
     }
   }
