@@ -473,6 +473,7 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
   p.n_slots = ns;
   const size_t smem = 1024 + p.r_off + (size_t)ns * SA_SLOT;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.out_v8 = aligned(out, 32) ? 1 : 0;  // rows are dv * 2 bytes (a multiple of 128), steps 32
   p.status = dev->status;
   p.budget_ns = wait_budget_ns();
   CUtensorMap qm;

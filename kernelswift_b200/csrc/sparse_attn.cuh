@@ -104,6 +104,7 @@ struct SaParams {
   int32_t idx_vec4;     // indices may be read as int4 (K % 4 == 0, 16-byte aligned)
   uint32_t q_off, p_off, r_off;  // query tile, P, ring
   float scale_log2;     // softmax_scale * log2(e)
+  int32_t out_v8;       // out is 32-byte aligned: 32-byte row stores
   int* status;
   uint64_t budget_ns;
 };
@@ -730,9 +731,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(SA_THREADS, 1)
 #pragma unroll
             for (int t = 0; t < 8; ++t)
               w[t] = cvt_bf16x2(__uint_as_float(o[2 * t]) * inv, __uint_as_float(o[2 * t + 1]) * inv);
-            uint4* dst = reinterpret_cast<uint4*>(orow + d0 + c);
-            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            if (p.out_v8) {  // one whole 32-byte sector per store
+              asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(orow + d0 + c),
+                           "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]),
+                           "r"(w[7])
+                           : "memory");
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(orow + d0 + c);
+              dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+              dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            }
           }
         }
         ocol += hn;
