@@ -892,6 +892,50 @@ def per_op_block(rank, world, local, device, barrier, peaks, target_s=0.4):
     return res
 
 
+# v1 latency the reference publishes for its own default inputs (Ascend 910B3; other
+# hardware, context only): optimized/sinkhorn_project/design.md:120-122,
+# optimized/sparse_attention/README.md:58-59, optimized/indexer_project/design.md:173-174
+REF_910B3_V1_MS = {"sinkhorn": 0.14, "sparse_attention": 0.92, "indexer": 1.741}
+
+
+def dropin_block(device, calls=200, warmup=20):
+    """The three drop-in ModelNew forwards at the reference's own default inputs
+    (each module's get_init_inputs / get_inputs, what the reference's harness
+    times), as its protocol measures them: warm-up, then the median of calls each
+    followed by a device synchronize (wall clock; the device span of each call,
+    CUDA events, beside it).  Each rank runs the whole inputs on its own GPU."""
+    import importlib
+    import torch
+
+    res = {}
+    for name in ("sinkhorn", "sparse_attention", "indexer"):
+        mod = importlib.import_module(f"kernelswift_b200.{name}")
+        torch.manual_seed(42)
+        model = mod.ModelNew(*mod.get_init_inputs()).to(device)
+        inputs = [x.to(device) if torch.is_tensor(x) else x for x in mod.get_inputs()]
+        wall, dev = [], []
+        with torch.no_grad():
+            for _ in range(warmup):
+                model(*inputs)
+            torch.cuda.synchronize()
+            for _ in range(calls):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                t0 = time.perf_counter()
+                e0.record()
+                model(*inputs)
+                e1.record()
+                torch.cuda.synchronize()
+                wall.append((time.perf_counter() - t0) * 1e6)
+                dev.append(e0.elapsed_time(e1) * 1e3)
+        res[name] = {"inputs": [list(x.shape) if torch.is_tensor(x) else x for x in inputs],
+                     "us_per_call": round(statistics.median(wall), 1),
+                     "device_us_per_call": round(statistics.median(dev), 1),
+                     "reference_910B3_v1_us": REF_910B3_V1_MS[name] * 1e3}
+        del model, inputs
+        torch.cuda.empty_cache()
+    return res
+
+
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -974,6 +1018,7 @@ def main():
         del wl
         torch.cuda.empty_cache()
         line["per_op"] = per_op_block(rank, world, local, device, barrier, peaks)
+        line["dropin"] = dropin_block(device)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
