@@ -421,14 +421,26 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
       sp.scale_log2 = scale * 1.4426950408889634f;
       sp.status = dev->status;
       sp.budget_ns = wait_budget_ns();
-      const void* fn = hn == 16 ? reinterpret_cast<const void*>(sparse_attn_small_kernel<16>)
-                     : hn == 32 ? reinterpret_cast<const void*>(sparse_attn_small_kernel<32>)
-                                : reinterpret_cast<const void*>(sparse_attn_small_kernel<64>);
+      // two warp groups for up to two key tiles, four (one per tile) beyond
+      const bool wide = nt > 2;
+      const void* fn =
+          wide ? (hn == 16 ? reinterpret_cast<const void*>(sparse_attn_small_kernel<16, 4>)
+                  : hn == 32 ? reinterpret_cast<const void*>(sparse_attn_small_kernel<32, 4>)
+                             : reinterpret_cast<const void*>(sparse_attn_small_kernel<64, 4>))
+               : (hn == 16 ? reinterpret_cast<const void*>(sparse_attn_small_kernel<16, 2>)
+                  : hn == 32 ? reinterpret_cast<const void*>(sparse_attn_small_kernel<32, 2>)
+                             : reinterpret_cast<const void*>(sparse_attn_small_kernel<64, 2>));
       if (int rc = smem_optin(dev, fn, "cudaFuncSetAttribute(sparse_attn_small)")) return rc;
       const unsigned grid = (unsigned)(B * M);
-      if (hn == 16) sparse_attn_small_kernel<16><<<grid, SAS_THREADS, smem, st>>>(sp);
-      else if (hn == 32) sparse_attn_small_kernel<32><<<grid, SAS_THREADS, smem, st>>>(sp);
-      else sparse_attn_small_kernel<64><<<grid, SAS_THREADS, smem, st>>>(sp);
+      if (wide) {
+        if (hn == 16) sparse_attn_small_kernel<16, 4><<<grid, 512, smem, st>>>(sp);
+        else if (hn == 32) sparse_attn_small_kernel<32, 4><<<grid, 512, smem, st>>>(sp);
+        else sparse_attn_small_kernel<64, 4><<<grid, 512, smem, st>>>(sp);
+      } else {
+        if (hn == 16) sparse_attn_small_kernel<16, 2><<<grid, 256, smem, st>>>(sp);
+        else if (hn == 32) sparse_attn_small_kernel<32, 2><<<grid, 256, smem, st>>>(sp);
+        else sparse_attn_small_kernel<64, 2><<<grid, 256, smem, st>>>(sp);
+      }
       return launch_check("sparse_attn_small_kernel launch");
     }
   }

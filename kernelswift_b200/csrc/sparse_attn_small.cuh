@@ -13,17 +13,20 @@
 // rescaling.  P is rounded to bf16 for the PV product and the normalisation is
 // applied in fp32 at the end, as in sparse_attn_kernel.
 //
-// One CTA of 256 threads: all 8 warps gather (cp.async, 16 bytes per copy, zeros
-// for masked keys); warp 4 issues the MMAs (one elected lane); warps 0-3 (TMEM lane
-// quarters) run the softmax over the S^T columns and the epilogue over O^T.
+// One CTA of 128 G threads (G = 2 warp groups for index rows of at most 256 keys,
+// 4 for longer ones): all warps gather (cp.async, 16 bytes per copy, zeros for
+// masked keys); warp 4 issues the MMAs (one elected lane); every warp group runs
+// the softmax over its own 128-key tiles of S^T (warp w reads TMEM lane quarter
+// w % 4), so the tiles of one token are worked on side by side, and the groups
+// share the epilogue's column blocks of O^T.
 #pragma once
 #include "ks_device.cuh"
 
 namespace ks {
 
-constexpr int SAS_THREADS = 256;
+constexpr int SAS_MAX_G = 4;     // warp groups of the widest CTA
 constexpr int SAS_MAX_K = 512;
-constexpr int SAS_HDR = 4096;
+constexpr int SAS_HDR = 7168;
 
 struct SaSmallParams {
   const uint16_t* q;    // bf16 [B, M, H, D]
@@ -47,16 +50,17 @@ struct SaSmallShared {
   uint32_t tmem_base;
   int abort;
   int oob;
-  float red[4][64];     // per-warp partial max / sum per head
+  float red[4 * SAS_MAX_G][64];  // per-warp partial max / sum per head
   float head_m[64];     // max per head (base-2 scaled), sink included
   float head_inv[64];   // 1 / denominator per head
   int32_t idx[SAS_MAX_K];  // the token's index row, -1 past K
 };
 static_assert(sizeof(SaSmallShared) <= SAS_HDR, "SaSmallShared exceeds its header");
 
-template <int HN>
-__global__ void __launch_bounds__(SAS_THREADS)
+template <int HN, int G>
+__global__ void __launch_bounds__(128 * G)
     sparse_attn_small_kernel(SaSmallParams p) {
+  constexpr int THREADS = 128 * G;
   extern __shared__ uint8_t sas_raw[];
   const uint32_t raw = smem_u32(sas_raw);
   uint8_t* smem = sas_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -88,12 +92,12 @@ __global__ void __launch_bounds__(SAS_THREADS)
   const int32_t* ip = p.idx + token * p.K;
   const uint16_t* kvb = p.kv + (int64_t)b * p.N * p.D;
   // the index row first (one coalesced pass), so no row copy waits on an index load
-  for (int k = threadIdx.x; k < K_pad; k += SAS_THREADS) sh->idx[k] = k < p.K ? __ldg(ip + k) : -1;
+  for (int k = threadIdx.x; k < K_pad; k += THREADS) sh->idx[k] = k < p.K ? __ldg(ip + k) : -1;
   __syncthreads();
   {
     const int pieces_per_row = p.nkb * 8;
     const int total = K_pad * pieces_per_row;
-    for (int e = threadIdx.x; e < total; e += SAS_THREADS) {
+    for (int e = threadIdx.x; e < total; e += THREADS) {
       const int k = e / pieces_per_row, c = e % pieces_per_row;
       const int32_t v = sh->idx[k];
       const bool ok = v >= 0 && v < p.N && c * 8 < p.D;
@@ -105,7 +109,7 @@ __global__ void __launch_bounds__(SAS_THREADS)
     // the query rows (heads) h < H of this token, zeros for the padding rows
     const uint16_t* qt = p.q + token * (int64_t)p.H * p.D;
     const int qpieces = HN * p.nkb * 8;
-    for (int e = threadIdx.x; e < qpieces; e += SAS_THREADS) {
+    for (int e = threadIdx.x; e < qpieces; e += THREADS) {
       const int h = e / (p.nkb * 8), c = e % (p.nkb * 8);
       const bool ok = h < p.H && c * 8 < p.D;
       uint8_t* dst = qs + (c >> 3) * (HN * 128) + h * 128 + (((c & 7) ^ (h & 7)) << 4);
@@ -138,106 +142,108 @@ __global__ void __launch_bounds__(SAS_THREADS)
     __syncwarp();
   }
 
-  // ---------------------------------------------------------------- softmax (warps 0-3)
-  // Thread = key (k = 32 warp + lane within each 128-key tile).  Heads go in
-  // groups of 16 TMEM columns; each pass re-reads S^T from TMEM, so registers do
-  // not grow with H or K.  Max and sum per head are reduced over the warp by a
-  // shuffle butterfly and over the four warps through shared memory.
-  if (warp < 4) {
-    const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->mma_bar, 0, wc));
-    uint32_t vmask = 0;  // bit t: this thread's key of tile t is valid
-    for (int t = 0; t < p.nt; ++t) {
-      const int32_t v = sh->idx[t * 128 + warp * 32 + lane];
-      vmask |= (uint32_t)(v >= 0 && v < p.N) << t;
-    }
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    if (ok) {
-      tc_fence_after();
-#pragma unroll 1
-      for (int hg = 0; hg < HN; hg += 16) {
-        float mh[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) mh[i] = -INFINITY;
-        for (int t = 0; t < p.nt; ++t) {
-          uint32_t r[16];
-          tmem_ld16(tmem + s_col + t * HN + hg + lane_off, r);
-          tmem_wait_ld();
-          if ((vmask >> t) & 1u) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) mh[i] = fmaxf(mh[i], __uint_as_float(r[i]) * p.scale_log2);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) mh[i] = fmaxf(mh[i], __shfl_xor_sync(0xFFFFFFFFu, mh[i], o));
-        }
-        if (lane == 0) {  // (after the butterfly every lane holds the warp's maxima)
-#pragma unroll
-          for (int i = 0; i < 16; ++i) sh->red[warp][hg + i] = mh[i];
-        }
-      }
-    }
-    named_bar_sync(1, 128);
-    if (ok && threadIdx.x < HN) {
-      const int h = threadIdx.x;
-      const float sink2 = h < p.H ? __ldg(p.sink + h) * 1.4426950408889634f : 0.f;
-      sh->head_m[h] = fmaxf(fmaxf(fmaxf(sh->red[0][h], sh->red[1][h]),
-                                  fmaxf(sh->red[2][h], sh->red[3][h])), sink2);
-    }
-    named_bar_sync(1, 128);
-    if (ok) {
-#pragma unroll 1
-      for (int hg = 0; hg < HN; hg += 16) {
-        float ls[16], hm[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          ls[i] = 0.f;
-          hm[i] = sh->head_m[hg + i];
-        }
-        for (int t = 0; t < p.nt; ++t) {
-          const int k = t * 128 + warp * 32 + lane;  // key of this thread in tile t
-          const bool valid = (vmask >> t) & 1u;
-          uint32_t r[16];
-          tmem_ld16(tmem + s_col + t * HN + hg + lane_off, r);
-          tmem_wait_ld();
-          const int kk = k & 63;
-          uint8_t* chunk = ps + (k >> 6) * (HN * 128);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int h = hg + i;
-            const float e = valid ? ex2f(fmaf(__uint_as_float(r[i]), p.scale_log2, -hm[i])) : 0.f;
-            ls[i] += e;
-            // P^T (K-major: row h holds the keys, 64 per 128-byte row): pairs of
-            // keys (even lane, odd lane) go out as one 32-bit store by the even lane
-            const float e_hi = __shfl_down_sync(0xFFFFFFFFu, e, 1);
-            if ((lane & 1) == 0)
-              *reinterpret_cast<uint32_t*>(chunk + h * 128 + (((kk >> 3) ^ (h & 7)) << 4) + (kk & 7) * 2) =
-                  cvt_bf16x2(e, e_hi);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) ls[i] += __shfl_xor_sync(0xFFFFFFFFu, ls[i], o);
-        }
-        if (lane == 0) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) sh->red[warp][hg + i] = ls[i];
-        }
-      }
-      fence_proxy_async_smem();  // P^T is read by the tensor cores next
-    }
-    named_bar_sync(1, 128);
-    if (ok && threadIdx.x < HN) {
-      const int h = threadIdx.x;
-      const float sink2 = h < p.H ? __ldg(p.sink + h) * 1.4426950408889634f : 0.f;
-      const float den = (sh->red[0][h] + sh->red[1][h]) + (sh->red[2][h] + sh->red[3][h]) +
-                        ex2f(sink2 - sh->head_m[h]);
-      sh->head_inv[h] = 1.f / den;
-    }
-    tc_fence_before();
+  // ---------------------------------------------------------------- softmax (all warps)
+  // Thread = key: warp w of group g = w / 4 takes keys 32 (w % 4) + lane of tiles
+  // g, g + G, ...  Heads go in groups of 16 TMEM columns; each pass re-reads S^T
+  // from TMEM, so registers do not grow with H or K.  Max and sum per head are
+  // reduced over the warp by a shuffle butterfly and over the warps through shared
+  // memory (warps without a tile contribute -inf / 0).
+  const int quarter = warp & 3, grp = warp >> 2;
+  const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+  const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->mma_bar, 0, wc));
+  uint32_t vmask = 0;  // bit t: this thread's key of tile t is valid
+  for (int t = grp; t < p.nt; t += G) {
+    const int32_t v = sh->idx[t * 128 + quarter * 32 + lane];
+    vmask |= (uint32_t)(v >= 0 && v < p.N) << t;
   }
+  if (ok) {
+    tc_fence_after();
+#pragma unroll 1
+    for (int hg = 0; hg < HN; hg += 16) {
+      float mh[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) mh[i] = -INFINITY;
+      for (int t = grp; t < p.nt; t += G) {
+        uint32_t r[16];
+        tmem_ld16(tmem + s_col + t * HN + hg + lane_off, r);
+        tmem_wait_ld();
+        if ((vmask >> t) & 1u) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) mh[i] = fmaxf(mh[i], __uint_as_float(r[i]) * p.scale_log2);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mh[i] = fmaxf(mh[i], __shfl_xor_sync(0xFFFFFFFFu, mh[i], o));
+      }
+      if (lane == 0) {  // (after the butterfly every lane holds the warp's maxima)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sh->red[warp][hg + i] = mh[i];
+      }
+    }
+  }
+  __syncthreads();
+  const float sink2 = threadIdx.x < p.H ? __ldg(p.sink + threadIdx.x) * 1.4426950408889634f : 0.f;
+  if (ok && threadIdx.x < HN) {
+    const int h = threadIdx.x;
+    float m = sink2;
+#pragma unroll
+    for (int w = 0; w < 4 * G; ++w) m = fmaxf(m, sh->red[w][h]);
+    sh->head_m[h] = m;
+  }
+  __syncthreads();
+  if (ok) {
+#pragma unroll 1
+    for (int hg = 0; hg < HN; hg += 16) {
+      float ls[16], hm[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        ls[i] = 0.f;
+        hm[i] = sh->head_m[hg + i];
+      }
+      for (int t = grp; t < p.nt; t += G) {
+        const int k = t * 128 + quarter * 32 + lane;  // key of this thread in tile t
+        const bool valid = (vmask >> t) & 1u;
+        uint32_t r[16];
+        tmem_ld16(tmem + s_col + t * HN + hg + lane_off, r);
+        tmem_wait_ld();
+        const int kk = k & 63;
+        uint8_t* chunk = ps + (k >> 6) * (HN * 128);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int h = hg + i;
+          const float e = valid ? ex2f(fmaf(__uint_as_float(r[i]), p.scale_log2, -hm[i])) : 0.f;
+          ls[i] += e;
+          // P^T (K-major: row h holds the keys, 64 per 128-byte row): pairs of
+          // keys (even lane, odd lane) go out as one 32-bit store by the even lane
+          const float e_hi = __shfl_down_sync(0xFFFFFFFFu, e, 1);
+          if ((lane & 1) == 0)
+            *reinterpret_cast<uint32_t*>(chunk + h * 128 + (((kk >> 3) ^ (h & 7)) << 4) + (kk & 7) * 2) =
+                cvt_bf16x2(e, e_hi);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ls[i] += __shfl_xor_sync(0xFFFFFFFFu, ls[i], o);
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sh->red[warp][hg + i] = ls[i];
+      }
+    }
+    fence_proxy_async_smem();  // P^T is read by the tensor cores next
+  }
+  __syncthreads();
+  if (ok && threadIdx.x < HN) {
+    const int h = threadIdx.x;
+    float den = ex2f(sink2 - sh->head_m[h]);
+#pragma unroll
+    for (int w = 0; w < 4 * G; ++w) den += sh->red[w][h];
+    sh->head_inv[h] = 1.f / den;
+  }
+  tc_fence_before();
   __syncthreads();
 
   // ---------------------------------------------------------------- P V
@@ -263,31 +269,29 @@ __global__ void __launch_bounds__(SAS_THREADS)
     __syncwarp();
   }
 
-  // ---------------------------------------------------------------- epilogue (warps 0-3)
+  // ---------------------------------------------------------------- epilogue (all warps)
   // Thread = output dim (TMEM lane) of each 128-dim tile; out[token, h, dim] for h < H.
-  if (warp < 4) {
-    if (__all_sync(0xFFFFFFFFu, mbar_wait(&sh->mma_bar, 1, wc))) {
-      tc_fence_after();
-      uint16_t* orow = p.out + token * (int64_t)p.H * p.dv;
-      for (int m = 0; m < p.dv_tiles; ++m) {
-        const int d = m * 128 + warp * 32 + lane;
+  // Block j = (tile m, 16 heads) goes to warp group j % G.
+  if (__all_sync(0xFFFFFFFFu, mbar_wait(&sh->mma_bar, 1, wc))) {
+    tc_fence_after();
+    uint16_t* orow = p.out + token * (int64_t)p.H * p.dv;
+    const int nblk = p.dv_tiles * (HN / 16);
+    for (int j = grp; j < nblk; j += G) {
+      const int m = j / (HN / 16), c = (j % (HN / 16)) * 16;
+      const int d = m * 128 + quarter * 32 + lane;
+      uint32_t r[16];
+      tmem_ld16(tmem + o_col + m * HN + c + lane_off, r);
+      tmem_wait_ld();
+      if (d < p.dv) {
 #pragma unroll
-        for (int c = 0; c < HN; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(tmem + o_col + m * HN + c + ((uint32_t)(warp * 32) << 16), r);
-          tmem_wait_ld();
-          if (d < p.dv) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (c + i < p.H)
-                orow[(int64_t)(c + i) * p.dv + d] =
-                    __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[i]) * sh->head_inv[c + i]));
-          }
-        }
+        for (int i = 0; i < 16; ++i)
+          if (c + i < p.H)
+            orow[(int64_t)(c + i) * p.dv + d] =
+                __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[i]) * sh->head_inv[c + i]));
       }
     }
-    if (threadIdx.x == 0 && sh->oob) report_bounds(p.status, (int)token, p.N);
   }
+  if (threadIdx.x == 0 && sh->oob) report_bounds(p.status, (int)token, p.N);
 
   tc_fence_before();
   __syncthreads();

@@ -243,3 +243,41 @@ def test_tiny_rows(cuda_ok, B, M, H, D, N, K, dv_begin, dv):
     ref = O.sparse_attn(bits_from_bf16(q), bits_from_bf16(kv), s.numpy(), idx.numpy(), D ** -0.5,
                         dv_begin + dv)[..., dv_begin:]
     assert_close(bits_from_bf16(out), ref)
+
+
+@pytest.mark.parametrize("B,M,H,D,N,K,dv_begin,dv", [
+    (1, 9, 16, 128, 900, 300, 0, 128),     # three tiles: a cluster of 4, the last CTA past K
+    (2, 5, 64, 256, 1000, 512, 0, 256),    # four full tiles, 64 heads, the widest output
+    (1, 6, 32, 192, 500, 200, 64, 128),    # two tiles, a column slice
+    (3, 4, 24, 128, 3000, 129, 0, 128),    # a single key in the second tile
+])
+def test_split_rows(cuda_ok, B, M, H, D, N, K, dv_begin, dv):
+    """Index rows of 129-512 keys with at most 64 heads: a cluster of 2 or 4 CTAs per
+    token, one 128-key tile each, maxima and sums exchanged and partial outputs
+    summed through distributed shared memory.  Rows with nothing valid, with keys in
+    one CTA's tile only, with the first tile empty and with one key repeated
+    against the oracle; repeated calls bit-identical (fixed combine order)."""
+    from kernelswift_b200 import _lib, ops
+
+    q, kv, s, idx = make_case(B, M, H, D, N, K, seed=51 + H + K, mode="mixed")
+    idx[0, 0] = -1
+    idx[0, 1, 128:] = -1
+    idx[0, 2, :128] = -1
+    idx[-1, -1, :] = idx[-1, -1, 0]
+    qc, kvc, sc, ic = q.cuda(), kv.cuda(), s.cuda(), idx.cuda()
+
+    def call():
+        out = torch.empty(B, M, H, dv, dtype=torch.bfloat16, device="cuda")
+        _lib.check(_lib.lib().ks_sparse_attn(qc.data_ptr(), kvc.data_ptr(), sc.data_ptr(), ic.data_ptr(),
+                                             out.data_ptr(), B, M, H, D, N, K, dv_begin, dv, D ** -0.5,
+                                             torch.cuda.current_stream().cuda_stream), "ks_sparse_attn")
+        return out
+
+    out = call()
+    ops.device_status()
+    ref = O.sparse_attn(bits_from_bf16(q), bits_from_bf16(kv), s.numpy(), idx.numpy(), D ** -0.5,
+                        dv_begin + dv)[..., dv_begin:]
+    assert_close(bits_from_bf16(out), ref)
+    assert torch.all(out[0, 0].float() == 0)  # nothing valid: the sink alone, zeros out
+    for _ in range(3):
+        assert torch.equal(out, call())
