@@ -379,15 +379,20 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
       while (tcols < std::max(ncol, (int)dv)) tcols <<= 1;
       tp.tmem_cols = (uint32_t)tcols;
       tp.scale_log2 = scale * 1.4426950408889634f;
-      tp.out_v8 = aligned(out, 32) ? 1 : 0;  // rows are dv * 2 bytes, a multiple of 128
+      const size_t smem = 1024 + SAT_HDR + kg_bytes + (size_t)q_chunks * 16384;
       tp.status = dev->status;
       tp.budget_ns = wait_budget_ns();
-      const size_t smem = 1024 + SAT_HDR + kg_bytes + (size_t)q_chunks * 16384;
+      CUtensorMap qm;  // q as [B M H rows, D], boxes of 64 dims x 128 rows
+      if (int rc = make_map_bf16(&qm, q, (uint64_t)D, (uint64_t)(B * M * H), (uint64_t)D * 2, 64, 128))
+        return rc;
+      CUtensorMap om;  // out as [B M H rows, dv], the same boxes
+      if (int rc = make_map_bf16(&om, out, (uint64_t)dv, (uint64_t)(B * M * H), (uint64_t)dv * 2, 64, 128))
+        return rc;
       if (int rc = smem_optin(dev, reinterpret_cast<const void*>(sparse_attn_tiny_kernel),
                               "cudaFuncSetAttribute(sparse_attn_tiny)"))
         return rc;
       const unsigned grid = (unsigned)((B * M + tpt - 1) / tpt);
-      sparse_attn_tiny_kernel<<<grid, SAT_THREADS, smem, st>>>(tp);
+      sparse_attn_tiny_kernel<<<grid, SAT_THREADS, smem, st>>>(qm, om, tp);
       return launch_check("sparse_attn_tiny_kernel launch");
     }
   }

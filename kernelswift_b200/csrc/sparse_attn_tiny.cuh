@@ -18,11 +18,13 @@
 // operand of PV: nothing is gathered twice.  P is rounded to bf16 for PV and the
 // normalisation applied in fp32 at the end, as in sparse_attn_kernel.
 //
-// One CTA of 128 threads per tile: all gather (cp.async, 16 bytes per copy, zeros
-// for masked keys and rows past the last token); one elected lane of warp 0 issues
-// the MMAs; thread t runs the softmax and the epilogue of row t.  P overwrites the
-// query tile (free once QK has completed) and O the score columns in TMEM (free
-// once the softmax has read them).
+// One CTA of 128 threads per tile: all gather the key rows (cp.async, 16 bytes per
+// copy, zeros for masked keys); the query tile comes by TMA (128-byte swizzle, rows
+// past the last token read as zeros) and the output tile leaves by TMA (staged over
+// P, rows past the last token clipped); one elected lane of warp 0 issues the MMAs;
+// thread t runs the softmax and the epilogue of row t.  P overwrites the query tile
+// (free once QK has completed) and O the score columns in TMEM (free once the
+// softmax has read them).
 #pragma once
 #include "sparse_attn.cuh"
 
@@ -45,13 +47,13 @@ struct SaTinyParams {
   uint32_t kg_off, q_off; // shared-memory regions (bytes from the aligned base)
   uint32_t tmem_cols;
   float scale_log2;
-  int32_t out_v8;       // out is 32-byte aligned: 32-byte row stores
   int* status;
   uint64_t budget_ns;
 };
 
 struct SaTinyShared {
   uint64_t mma_bar;
+  uint64_t q_bar;       // the query tile's TMA loads
   uint32_t tmem_base;
   int abort;
   int oob;
@@ -61,21 +63,28 @@ struct SaTinyShared {
 static_assert(sizeof(SaTinyShared) <= SAT_HDR, "SaTinyShared exceeds its header");
 
 __global__ void __launch_bounds__(SAT_THREADS)
-    sparse_attn_tiny_kernel(SaTinyParams p) {
+    sparse_attn_tiny_kernel(const __grid_constant__ CUtensorMap qmap,
+                            const __grid_constant__ CUtensorMap omap, SaTinyParams p) {
   extern __shared__ uint8_t sat_raw[];
   const uint32_t raw = smem_u32(sat_raw);
   uint8_t* smem = sat_raw + (((raw + 1023u) & ~1023u) - raw);
   SaTinyShared* sh = reinterpret_cast<SaTinyShared*>(smem);
   uint8_t* kg = smem + p.kg_off;  // [nkb][ncol rows x 128 B], 128-byte swizzle
   uint8_t* qs = smem + p.q_off;   // [nkb][128 rows x 128 B]; later P [ncol / 64][128 rows x 128 B]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int64_t n_tok = (int64_t)p.B * p.M;
   const int64_t tok0 = (int64_t)blockIdx.x * p.tpt;  // first token of the tile
   const int64_t row0 = tok0 * p.H;                   // first q / out row of the tile
-  const int64_t n_rows = n_tok * p.H;
   const uint32_t chunk = (uint32_t)p.ncol * 128u;    // bytes of one 64-dim chunk of kg
   WaitCtx wc{&sh->abort, p.status, p.budget_ns};
 
+  // the query tile first: it depends on nothing, and one thread issues it
+  if (threadIdx.x == 0) {
+    mbar_init(&sh->q_bar, 1);
+    fence_barrier_init();
+    mbar_expect_tx(&sh->q_bar, (uint32_t)p.nkb * 16384u);
+    for (int kb = 0; kb < p.nkb; ++kb) tma_load_2d(&qmap, &sh->q_bar, qs + kb * 16384, kb * 64, (int32_t)row0);
+  }
   // the index rows of the tile's tokens (-1 for slots past K and tokens past the
   // end), loaded before the set-up so their latency overlaps it; every copy then
   // reads its row from shared memory (ncol <= 2 x 128)
@@ -120,13 +129,6 @@ __global__ void __launch_bounds__(SAT_THREADS)
       uint8_t* dst = kg + (c >> 3) * chunk + r * 128 + (((c & 7) ^ (r & 7)) << 4);
       cp_async16(dst, ok ? src : p.kv, ok ? 16u : 0u);
     }
-    // the tile's 128 query rows (zeros past the last token)
-    for (int e = threadIdx.x; e < 128 * pieces; e += SAT_THREADS) {
-      const int r = e / pieces, c = e - r * pieces;
-      const bool ok = row0 + r < n_rows;
-      uint8_t* dst = qs + (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
-      cp_async16(dst, ok ? p.q + (row0 + r) * p.D + c * 8 : p.q, ok ? 16u : 0u);
-    }
     cp_async_wait_all();
     fence_proxy_async_smem();
   }
@@ -136,7 +138,8 @@ __global__ void __launch_bounds__(SAT_THREADS)
   const uint32_t tmem = sh->tmem_base;
 
   // ---------------------------------------------------------------- S = Q Kg^T
-  if (warp == 0) {
+  if (warp == 0 && __all_sync(0xFFFFFFFFu, mbar_wait(&sh->q_bar, 0, wc))) {
+    tc_fence_after();
     if (elect_one()) {
       const uint32_t idesc = idesc_bf16_f32(128, p.ncol, false, false);
       for (int ks = 0; ks < p.D / 16; ++ks) {
@@ -154,8 +157,6 @@ __global__ void __launch_bounds__(SAT_THREADS)
   // its own token, c0 .. c0 + kp)
   const int r = threadIdx.x;
   const int j = r / p.H, h = r - j * p.H;
-  const int64_t row = row0 + r;
-  const bool live = row < n_rows;
   const int c0 = j * p.kp;
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
   const float sink2 = __ldg(p.sink + h) * 1.4426950408889634f;
@@ -223,11 +224,13 @@ __global__ void __launch_bounds__(SAT_THREADS)
   }
 
   // ---------------------------------------------------------------- epilogue of row r
+  // Row r's dv outputs go to shared memory (over P, which the completed PV no longer
+  // reads) in 64-column chunks with the 128-byte swizzle; one thread then stores the
+  // tile with TMA (rows past the last token are clipped by the tensor map).
   if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->mma_bar, 1, wc));
   if (ok) {
     tc_fence_after();
     const float inv = 1.f / (lsum + ex2f(sink2 - m));
-    uint16_t* orow = p.out + row * p.dv;
     for (int cc = 0; cc < p.dv; cc += 16) {
       uint32_t o[16];
       tmem_ld16(tmem + lane_off + cc, o);
@@ -236,21 +239,22 @@ __global__ void __launch_bounds__(SAT_THREADS)
 #pragma unroll
       for (int t = 0; t < 8; ++t)
         w[t] = cvt_bf16x2(__uint_as_float(o[2 * t]) * inv, __uint_as_float(o[2 * t + 1]) * inv);
-      if (live) {
-        if (p.out_v8) {  // one whole 32-byte sector per store
-          asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(orow + cc),
-                       "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]),
-                       "r"(w[7])
-                       : "memory");
-        } else {
-          uint4* dst = reinterpret_cast<uint4*>(orow + cc);
-          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        }
-      }
+      uint8_t* orow = qs + (cc >> 6) * 16384 + r * 128;
+      const int u0 = (cc & 63) >> 3;
+      *reinterpret_cast<uint4*>(orow + ((u0 ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(orow + (((u0 + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
     }
+    fence_proxy_async_smem();  // read by the TMA store next
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !sh->abort) {
+    for (int kb = 0; kb < p.dv / 64; ++kb) tma_store_2d(&omap, qs + kb * 16384, kb * 64, (int32_t)row0);
+    bulk_commit_group();
+    bulk_wait_group_read<0>();  // the staging area may be released once read
   }
   if (threadIdx.x == 0 && sh->oob) report_bounds(p.status, (int)tok0, p.N);
+  // (no TMA write may be in flight when the CTA leaves, also after a timeout)
+  if (threadIdx.x == 0) mbar_wait(&sh->q_bar, 0, wc, false, true);
 
   tc_fence_before();
   __syncthreads();

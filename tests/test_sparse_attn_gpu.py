@@ -224,11 +224,13 @@ def test_persistent_token_sequences(cuda_ok, K):
     (3, 13, 16, 128, 500, 32, 0, 128),    # 8 tokens per tile, tiles across batches
     (2, 9, 32, 256, 300, 20, 64, 192),    # 4 tokens per tile, a column slice
     (1, 7, 128, 256, 777, 64, 0, 256),    # one token per tile, the longest rows
+    (1, 5, 64, 128, 300, 16, 64, 64),     # TMA-stored tiles, the last half full, a column slice
 ])
 def test_tiny_rows(cuda_ok, B, M, H, D, N, K, dv_begin, dv):
     """Index rows of at most 64 keys: 128 / H tokens share one 128-row tile, each
     row keeping its own token's keys.  Duplicates, -1 entries, fully masked rows
-    and output column slices against the oracle."""
+    and output column slices against the oracle; the output tiles are stored by
+    TMA, the last one clipped where it runs past the last token."""
     from kernelswift_b200 import _lib, ops
 
     q, kv, s, idx = make_case(B, M, H, D, N, K, seed=41 + H + K, mode="mixed")
