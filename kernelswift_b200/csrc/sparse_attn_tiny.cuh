@@ -153,18 +153,22 @@ __global__ void __launch_bounds__(SAT_THREADS)
   }
 
   // ---------------------------------------------------------------- softmax of row r
-  // (TMEM loads are warp-wide: every lane reads all ncol columns and keeps those of
-  // its own token, c0 .. c0 + kp)
+  // (TMEM loads are warp-wide: every lane reads its warp's tokens' columns and keeps
+  // those of its own token, c0 .. c0 + kp)
   const int r = threadIdx.x;
   const int j = r / p.H, h = r - j * p.H;
   const int c0 = j * p.kp;
+  // the key columns of the warp's tokens (one token for H >= 32, two for H = 16):
+  // the only ones its rows can keep, so the only ones it loads from TMEM
+  const int cw0 = (warp * 32 / p.H) * p.kp;
+  const int cw1 = min(p.ncol, ((warp * 32 + 31) / p.H + 1) * p.kp);
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
   const float sink2 = __ldg(p.sink + h) * 1.4426950408889634f;
   float m = sink2, lsum = 0.f;
   bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sh->mma_bar, 0, wc));
   if (ok) {
     tc_fence_after();
-    for (int cc = 0; cc < p.ncol; cc += 16) {
+    for (int cc = cw0; cc < cw1; cc += 16) {
       uint32_t s[16];
       tmem_ld16(tmem + lane_off + cc, s);
       tmem_wait_ld();
@@ -178,22 +182,24 @@ __global__ void __launch_bounds__(SAT_THREADS)
     // P row r (K-major, 64 columns per 128-byte row of a 16 KB chunk, swizzled),
     // written over the query tile, which the completed QK no longer reads
     for (int cc = 0; cc < p.ncol; cc += 16) {
-      uint32_t s[16];
-      tmem_ld16(tmem + lane_off + cc, s);
-      tmem_wait_ld();
-      uint32_t pk[8];
+      uint32_t pk[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};  // other tokens' columns: P = 0
+      if (cc >= cw0 && cc < cw1) {
+        uint32_t s[16];
+        tmem_ld16(tmem + lane_off + cc, s);
+        tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        float e[2];
+        for (int i = 0; i < 16; i += 2) {
+          float e[2];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int c = cc + i + u;
-          const int32_t v = sh->idx[c];
-          const bool valid = c >= c0 && c < c0 + p.kp && v >= 0 && v < p.N;
-          e[u] = valid ? ex2f(fmaf(__uint_as_float(s[i + u]), p.scale_log2, -m)) : 0.f;
-          lsum += e[u];
+          for (int u = 0; u < 2; ++u) {
+            const int c = cc + i + u;
+            const int32_t v = sh->idx[c];
+            const bool valid = c >= c0 && c < c0 + p.kp && v >= 0 && v < p.N;
+            e[u] = valid ? ex2f(fmaf(__uint_as_float(s[i + u]), p.scale_log2, -m)) : 0.f;
+            lsum += e[u];
+          }
+          pk[i >> 1] = cvt_bf16x2(e[0], e[1]);
         }
-        pk[i >> 1] = cvt_bf16x2(e[0], e[1]);
       }
       uint8_t* prow = qs + (cc >> 6) * 16384 + r * 128;
       const int u0 = (cc & 63) >> 3;
