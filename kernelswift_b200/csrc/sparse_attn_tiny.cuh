@@ -58,6 +58,7 @@ struct SaTinyShared {
   int abort;
   int oob;
   int32_t idx[SAT_MAX_N];  // column c -> kv row (-1: masked slot)
+  uint32_t vmask[SAT_MAX_N / 32];  // bit c % 32 of word c / 32: column c holds a valid row
   int32_t bat[SAT_MAX_N / 16 + 8];  // batch of each token slot of the tile
 };
 static_assert(sizeof(SaTinyShared) <= SAT_HDR, "SaTinyShared exceeds its header");
@@ -107,8 +108,14 @@ __global__ void __launch_bounds__(SAT_THREADS)
     tmem_relinquish<1>();
   }
 #pragma unroll
-  for (int u = 0; u < 2; ++u)
-    if (threadIdx.x + u * SAT_THREADS < p.ncol) sh->idx[threadIdx.x + u * SAT_THREADS] = ix[u];
+  for (int u = 0; u < 2; ++u) {
+    const int c = threadIdx.x + u * SAT_THREADS;
+    const uint32_t vb = __ballot_sync(0xFFFFFFFFu, ix[u] >= 0 && ix[u] < p.N);
+    if (c < p.ncol) {
+      sh->idx[c] = ix[u];
+      if ((threadIdx.x & 31) == 0) sh->vmask[c >> 5] = vb;
+    }
+  }
   for (int j = threadIdx.x; j < p.tpt; j += SAT_THREADS) {
     const int64_t tok = tok0 + j;
     sh->bat[j] = tok < n_tok ? (int)(tok / p.M) : 0;
@@ -171,13 +178,13 @@ __global__ void __launch_bounds__(SAT_THREADS)
     for (int cc = cw0; cc < cw1; cc += 16) {
       uint32_t s[16];
       tmem_ld16(tmem + lane_off + cc, s);
+      // valid columns of this 16-column group that belong to the row's token (kp
+      // and c0 are multiples of 16: a group is wholly the row's token or not)
+      const uint32_t gm = (cc >= c0 && cc < c0 + p.kp) ? (sh->vmask[cc >> 5] >> (cc & 31)) & 0xFFFFu : 0u;
       tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int c = cc + i;
-        const int32_t v = sh->idx[c];
-        if (c >= c0 && c < c0 + p.kp && v >= 0 && v < p.N) m = fmaxf(m, __uint_as_float(s[i]) * p.scale_log2);
-      }
+      for (int i = 0; i < 16; ++i)
+        if ((gm >> i) & 1u) m = fmaxf(m, __uint_as_float(s[i]) * p.scale_log2);
     }
     // P row r (K-major, 64 columns per 128-byte row of a 16 KB chunk, swizzled),
     // written over the query tile, which the completed QK no longer reads
@@ -186,16 +193,14 @@ __global__ void __launch_bounds__(SAT_THREADS)
       if (cc >= cw0 && cc < cw1) {
         uint32_t s[16];
         tmem_ld16(tmem + lane_off + cc, s);
+        const uint32_t gm = (cc >= c0 && cc < c0 + p.kp) ? (sh->vmask[cc >> 5] >> (cc & 31)) & 0xFFFFu : 0u;
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
           float e[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
-            const int c = cc + i + u;
-            const int32_t v = sh->idx[c];
-            const bool valid = c >= c0 && c < c0 + p.kp && v >= 0 && v < p.N;
-            e[u] = valid ? ex2f(fmaf(__uint_as_float(s[i + u]), p.scale_log2, -m)) : 0.f;
+            e[u] = ((gm >> (i + u)) & 1u) ? ex2f(fmaf(__uint_as_float(s[i + u]), p.scale_log2, -m)) : 0.f;
             lsum += e[u];
           }
           pk[i >> 1] = cvt_bf16x2(e[0], e[1]);
