@@ -57,6 +57,37 @@ struct SaSmallShared {
 };
 static_assert(sizeof(SaSmallShared) <= SAS_HDR, "SaSmallShared exceeds its header");
 
+// Max (MX) or sum of v[i] over the warp's 32 lanes for 16 values i at once, by
+// halving exchanges: at offset 16 a lane sends the half of its values that its
+// partner keeps (8 shuffles), then 4, 2 and 1 at offsets 8, 4, 2, and a last
+// shuffle at offset 1 -- 16 shuffles instead of 16 x 5.  Lane L ends with the
+// result for i = (L >> 1) & 15.  Every value goes through the same pairwise tree
+// as a butterfly per value (v[L] op v[L ^ 16], then with L ^ 8, ...), so results
+// are bit-identical to it.
+template <bool MX>
+__device__ __forceinline__ float reduce16_lanes(const float (&v)[16], int lane) {
+  auto op = [](float a, float b) { return MX ? fmaxf(a, b) : a + b; };
+  float w[8], x[4], y[2];
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float keep = b4 ? v[j + 8] : v[j];
+    w[j] = op(keep, __shfl_xor_sync(0xFFFFFFFFu, b4 ? v[j] : v[j + 8], 16));
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float keep = b3 ? w[j + 4] : w[j];
+    x[j] = op(keep, __shfl_xor_sync(0xFFFFFFFFu, b3 ? w[j] : w[j + 4], 8));
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float keep = b2 ? x[j + 2] : x[j];
+    y[j] = op(keep, __shfl_xor_sync(0xFFFFFFFFu, b2 ? x[j] : x[j + 2], 4));
+  }
+  const float z = op(b1 ? y[1] : y[0], __shfl_xor_sync(0xFFFFFFFFu, b1 ? y[0] : y[1], 2));
+  return op(z, __shfl_xor_sync(0xFFFFFFFFu, z, 1));
+}
+
 template <int HN, int G>
 __global__ void __launch_bounds__(128 * G)
     sparse_attn_small_kernel(SaSmallParams p) {
@@ -97,8 +128,14 @@ __global__ void __launch_bounds__(128 * G)
   {
     const int pieces_per_row = p.nkb * 8;
     const int total = K_pad * pieces_per_row;
-    for (int e = threadIdx.x; e < total; e += THREADS) {
-      const int k = e / pieces_per_row, c = e % pieces_per_row;
+    // (key, piece) of element e, advanced by THREADS elements per step without a division
+    const int dk = THREADS / pieces_per_row, dc = THREADS - dk * pieces_per_row;
+    int k = threadIdx.x / pieces_per_row, c = threadIdx.x - k * pieces_per_row;
+    for (int e = threadIdx.x; e < total; e += THREADS, k += dk, c += dc) {
+      if (c >= pieces_per_row) {
+        c -= pieces_per_row;
+        ++k;
+      }
       const int32_t v = sh->idx[k];
       const bool ok = v >= 0 && v < p.N && c * 8 < p.D;
       if (k < p.K && v >= p.N) sh->oob = 1;
@@ -172,15 +209,8 @@ __global__ void __launch_bounds__(128 * G)
           for (int i = 0; i < 16; ++i) mh[i] = fmaxf(mh[i], __uint_as_float(r[i]) * p.scale_log2);
         }
       }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mh[i] = fmaxf(mh[i], __shfl_xor_sync(0xFFFFFFFFu, mh[i], o));
-      }
-      if (lane == 0) {  // (after the butterfly every lane holds the warp's maxima)
-#pragma unroll
-        for (int i = 0; i < 16; ++i) sh->red[warp][hg + i] = mh[i];
-      }
+      const float rm = reduce16_lanes<true>(mh, lane);  // head hg + (lane >> 1)
+      if ((lane & 1) == 0) sh->red[warp][hg + (lane >> 1)] = rm;
     }
   }
   __syncthreads();
@@ -223,15 +253,8 @@ __global__ void __launch_bounds__(128 * G)
                 cvt_bf16x2(e, e_hi);
         }
       }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ls[i] += __shfl_xor_sync(0xFFFFFFFFu, ls[i], o);
-      }
-      if (lane == 0) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) sh->red[warp][hg + i] = ls[i];
-      }
+      const float rs = reduce16_lanes<false>(ls, lane);
+      if ((lane & 1) == 0) sh->red[warp][hg + (lane >> 1)] = rs;
     }
     fence_proxy_async_smem();  // P^T is read by the tensor cores next
   }
