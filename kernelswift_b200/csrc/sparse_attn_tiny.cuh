@@ -56,10 +56,8 @@ struct SaTinyShared {
   uint64_t q_bar;       // the query tile's TMA loads
   uint32_t tmem_base;
   int abort;
-  int oob;
-  int32_t idx[SAT_MAX_N];  // column c -> kv row (-1: masked slot)
+  int32_t idx[SAT_MAX_N];  // column c -> row of kv as [B N, D] (batch folded in; -1: masked slot)
   uint32_t vmask[SAT_MAX_N / 32];  // bit c % 32 of word c / 32: column c holds a valid row
-  int32_t bat[SAT_MAX_N / 16 + 8];  // batch of each token slot of the tile
 };
 static_assert(sizeof(SaTinyShared) <= SAT_HDR, "SaTinyShared exceeds its header");
 
@@ -89,50 +87,57 @@ __global__ void __launch_bounds__(SAT_THREADS)
   // the index rows of the tile's tokens (-1 for slots past K and tokens past the
   // end), loaded before the set-up so their latency overlaps it; every copy then
   // reads its row from shared memory (ncol <= 2 x 128)
-  int32_t ix[2];
+  int32_t ix[2], tk[2];
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     const int c = threadIdx.x + u * SAT_THREADS;
     const int j = c / p.kp, i = c - j * p.kp;
     const int64_t tok = tok0 + j;
+    tk[u] = (int32_t)tok;  // < B M < 2^31 where it is used
     ix[u] = (c < p.ncol && i < p.K && tok < n_tok) ? __ldg(p.idx + tok * p.K + i) : -1;
   }
   if (threadIdx.x == 0) {
     mbar_init(&sh->mma_bar, 1);
     sh->abort = 0;
-    sh->oob = 0;
     fence_barrier_init();
   }
   if (warp == 0) {
     tmem_alloc<1>(&sh->tmem_base, p.tmem_cols);
     tmem_relinquish<1>();
   }
+  // each column's row of kv seen as [B N, D] (its token's batch folded in, so no
+  // copy below divides), the columns' validity bits, and whether any index is >= N
+  bool oob = false;
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     const int c = threadIdx.x + u * SAT_THREADS;
-    const uint32_t vb = __ballot_sync(0xFFFFFFFFu, ix[u] >= 0 && ix[u] < p.N);
+    const bool valid = ix[u] >= 0 && ix[u] < p.N;
+    const uint32_t vb = __ballot_sync(0xFFFFFFFFu, valid);
+    oob |= ix[u] >= p.N;
     if (c < p.ncol) {
-      sh->idx[c] = ix[u];
+      sh->idx[c] = valid ? (tk[u] / p.M) * p.N + ix[u] : -1;  // B N < 2^31
       if ((threadIdx.x & 31) == 0) sh->vmask[c >> 5] = vb;
     }
   }
-  for (int j = threadIdx.x; j < p.tpt; j += SAT_THREADS) {
-    const int64_t tok = tok0 + j;
-    sh->bat[j] = tok < n_tok ? (int)(tok / p.M) : 0;
-  }
-  __syncthreads();
+  oob = __syncthreads_or(oob);
 
   // ---------------------------------------------------------------- gathers
   {
     // key rows: piece c (16 bytes) of column r lands in chunk c / 8, row r,
     // 16-byte unit (c % 8) ^ (r % 8); masked slots are zero-filled
+    // (column r, piece c) of element e, advanced by the block size per step without
+    // a division
     const int pieces = p.nkb * 8;
-    for (int e = threadIdx.x; e < p.ncol * pieces; e += SAT_THREADS) {
-      const int r = e / pieces, c = e - r * pieces;
+    const int dr = SAT_THREADS / pieces, dc = SAT_THREADS - dr * pieces;
+    int r = threadIdx.x / pieces, c = threadIdx.x - r * pieces;
+    for (int e = threadIdx.x; e < p.ncol * pieces; e += SAT_THREADS, r += dr, c += dc) {
+      if (c >= pieces) {
+        c -= pieces;
+        ++r;
+      }
       const int32_t v = sh->idx[r];
-      const bool ok = v >= 0 && v < p.N;
-      if (v >= p.N) sh->oob = 1;
-      const uint16_t* src = p.kv + ((int64_t)sh->bat[r / p.kp] * p.N + (ok ? v : 0)) * p.D + c * 8;
+      const bool ok = v >= 0;
+      const uint16_t* src = p.kv + (int64_t)(ok ? v : 0) * p.D + c * 8;
       uint8_t* dst = kg + (c >> 3) * chunk + r * 128 + (((c & 7) ^ (r & 7)) << 4);
       cp_async16(dst, ok ? src : p.kv, ok ? 16u : 0u);
     }
@@ -263,7 +268,7 @@ __global__ void __launch_bounds__(SAT_THREADS)
     bulk_commit_group();
     bulk_wait_group_read<0>();  // the staging area may be released once read
   }
-  if (threadIdx.x == 0 && sh->oob) report_bounds(p.status, (int)tok0, p.N);
+  if (threadIdx.x == 0 && oob) report_bounds(p.status, (int)tok0, p.N);
   // (no TMA write may be in flight when the CTA leaves, also after a timeout)
   if (threadIdx.x == 0) mbar_wait(&sh->q_bar, 0, wc, false, true);
 

@@ -283,3 +283,23 @@ def test_split_rows(cuda_ok, B, M, H, D, N, K, dv_begin, dv):
     assert torch.all(out[0, 0].float() == 0)  # nothing valid: the sink alone, zeros out
     for _ in range(3):
         assert torch.equal(out, call())
+
+
+def test_tiny_out_of_range_index_reported(cuda_ok):
+    """The short-row kernel (128 / H tokens per tile) skips an index >= N like -1 and
+    reports it as a bounds error, as the other attention kernels do."""
+    from kernelswift_b200 import _lib, ops
+
+    B, M, H, D, N, K = 2, 5, 64, 128, 300, 16
+    q, kv, s, idx = make_case(B, M, H, D, N, K, seed=61)
+    bad = idx.clone()
+    bad[1, 3, 7] = N
+    out = ops.sparse_attn(q.cuda(), kv.cuda(), s.cuda(), bad.cuda(), D ** -0.5)
+    with pytest.raises(_lib.KsError) as e:
+        ops.device_status()
+    assert e.value.code == _lib.KS_ERR_DEVICE and "table size" in str(e.value)
+    ops.device_status()  # cleared
+    masked = bad.clone()
+    masked[masked >= N] = -1
+    ref = O.sparse_attn(bits_from_bf16(q), bits_from_bf16(kv), s.numpy(), masked.numpy(), D ** -0.5)
+    assert_close(bits_from_bf16(out), ref)
