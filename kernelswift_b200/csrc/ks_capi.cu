@@ -370,6 +370,7 @@ int sparse_attn_impl(const void* q, const void* kv, const float* sink, const int
       tp.B = (int)B; tp.M = (int)M; tp.H = (int)H; tp.D = (int)D; tp.N = (int)N; tp.K = (int)K;
       tp.dv_begin = (int)dv_begin; tp.dv = (int)dv;
       tp.tpt = tpt; tp.kp = kp; tp.ncol = ncol;
+      tp.inv_kp = 1.0f / (float)kp;
       tp.nkb = (int)(D / 64);
       const size_t kg_bytes = (size_t)tp.nkb * ncol * 128;          // a multiple of 1 KB
       const int q_chunks = std::max(tp.nkb, (ncol + 63) / 64);      // Q, then P

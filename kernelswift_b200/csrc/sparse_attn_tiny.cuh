@@ -43,6 +43,7 @@ struct SaTinyParams {
   uint16_t* out;        // bf16 [B, M, H, dv]
   int32_t B, M, H, D, N, K, dv_begin, dv;
   int32_t tpt, kp, ncol;  // tokens per tile, key slots per token, ncol = tpt * kp
+  float inv_kp;           // 1 / kp
   int32_t nkb;            // 64-dim chunks of D
   uint32_t kg_off, q_off; // shared-memory regions (bytes from the aligned base)
   uint32_t tmem_cols;
@@ -87,14 +88,26 @@ __global__ void __launch_bounds__(SAT_THREADS)
   // the index rows of the tile's tokens (-1 for slots past K and tokens past the
   // end), loaded before the set-up so their latency overlaps it; every copy then
   // reads its row from shared memory (ncol <= 2 x 128)
-  int32_t ix[2], tk[2];
+  // Column c is slot i of token j = c / kp: (c + 1/2) / kp in fp32 floors to j
+  // exactly (c < 256, kp <= 64: the rounding error is far below 1 / (2 kp)).  The
+  // token's batch comes from the tile's first token (one division) and carries.
+  int32_t ix[2], bt[2];
+  const int t0 = (int)tok0;  // tokens < B M < 2^30
+  const int b0 = t0 / p.M, m0 = t0 - b0 * p.M;
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     const int c = threadIdx.x + u * SAT_THREADS;
-    const int j = c / p.kp, i = c - j * p.kp;
+    const int j = (int)(((float)c + 0.5f) * p.inv_kp), i = c - j * p.kp;
     const int64_t tok = tok0 + j;
-    tk[u] = (int32_t)tok;  // < B M < 2^31 where it is used
-    ix[u] = (c < p.ncol && i < p.K && tok < n_tok) ? __ldg(p.idx + tok * p.K + i) : -1;
+    const bool live = c < p.ncol && i < p.K && tok < n_tok;
+    ix[u] = live ? __ldg(p.idx + tok * p.K + i) : -1;
+    int bb = b0, mm = m0 + j;
+    if (live)
+      while (mm >= p.M) {  // at most tpt - 1 steps
+        mm -= p.M;
+        ++bb;
+      }
+    bt[u] = bb;
   }
   if (threadIdx.x == 0) {
     mbar_init(&sh->mma_bar, 1);
@@ -115,7 +128,7 @@ __global__ void __launch_bounds__(SAT_THREADS)
     const uint32_t vb = __ballot_sync(0xFFFFFFFFu, valid);
     oob |= ix[u] >= p.N;
     if (c < p.ncol) {
-      sh->idx[c] = valid ? (tk[u] / p.M) * p.N + ix[u] : -1;  // B N < 2^31
+      sh->idx[c] = valid ? bt[u] * p.N + ix[u] : -1;  // B N < 2^31
       if ((threadIdx.x & 31) == 0) sh->vmask[c >> 5] = vb;
     }
   }
