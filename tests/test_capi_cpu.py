@@ -41,3 +41,17 @@ def test_workspace_size_is_host_only(built_lib):
     lib = _lib.lib()
     assert lib.ks_indexer_workspace_size(2, 32768, 32768) == 2 * 32768 * 32768 * 2
     assert lib.ks_indexer_workspace_size(1, 3, 5) % 256 == 0
+
+
+def test_tiny_attention_column_token_floor():
+    """The short-row attention kernel (csrc/sparse_attn_tiny.cuh) finds a key
+    column's token as floor((c + 1/2) * fp32(1 / kp)) instead of c / kp.  Exact for
+    every column c < 256 (SAT_MAX_N) and every slot count it takes (kp = K rounded
+    up to 16, K <= 64), with fp32 round-to-nearest as on the GPU."""
+    import numpy as np
+
+    for kp in (16, 32, 48, 64):
+        inv = np.float32(1.0) / np.float32(kp)
+        c = np.arange(256, dtype=np.float32)
+        j = np.floor((c + np.float32(0.5)) * inv).astype(np.int64)
+        assert np.array_equal(j, np.arange(256) // kp)
