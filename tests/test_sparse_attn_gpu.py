@@ -248,17 +248,17 @@ def test_tiny_rows(cuda_ok, B, M, H, D, N, K, dv_begin, dv):
 
 
 @pytest.mark.parametrize("B,M,H,D,N,K,dv_begin,dv", [
-    (1, 9, 16, 128, 900, 300, 0, 128),     # three tiles: a cluster of 4, the last CTA past K
+    (1, 9, 16, 128, 900, 300, 0, 128),     # three tiles: the 512-thread form, slots past K
     (2, 5, 64, 256, 1000, 512, 0, 256),    # four full tiles, 64 heads, the widest output
     (1, 6, 32, 192, 500, 200, 64, 128),    # two tiles, a column slice
     (3, 4, 24, 128, 3000, 129, 0, 128),    # a single key in the second tile
 ])
-def test_split_rows(cuda_ok, B, M, H, D, N, K, dv_begin, dv):
-    """Index rows of 129-512 keys with at most 64 heads: a cluster of 2 or 4 CTAs per
-    token, one 128-key tile each, maxima and sums exchanged and partial outputs
-    summed through distributed shared memory.  Rows with nothing valid, with keys in
-    one CTA's tile only, with the first tile empty and with one key repeated
-    against the oracle; repeated calls bit-identical (fixed combine order)."""
+def test_multi_tile_rows(cuda_ok, B, M, H, D, N, K, dv_begin, dv):
+    """Index rows of 129-512 keys with at most 64 heads (the few-heads kernel, one
+    warp group per 128-key tile, per-head maxima and sums combined across the
+    groups).  Rows with nothing valid, with keys in the first tile only, with the
+    first tile empty and with one key repeated against the oracle; repeated calls
+    bit-identical."""
     from kernelswift_b200 import _lib, ops
 
     q, kv, s, idx = make_case(B, M, H, D, N, K, seed=51 + H + K, mode="mixed")
